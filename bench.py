@@ -1,0 +1,474 @@
+"""Benchmark: draft-tree cycles/sec at batch 64 per GPU (score + build + GDN
+verify + commit), with roofline, CPU baseline and end-to-end numbers.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one full cycle over the batch (see dforktree_b200/cycle.py):
+score+build of 64 requests (S=24 positions over V=248,320 fp32 logits, the
+config-0 n-gram table shared), tree conv + GDN tree verify on each of the 24
+GDN layers of the Qwen3.5-9B shape (Hk=16, Hv=32, D=128), greedy tree
+acceptance against synthetic target tokens (accepted lengths uniform 1..24),
+and the closed-form commit of every layer's state.  Data is synthetic (seeded;
+random-init layer weights).  Under torchrun every rank runs its own batch of
+64 requests (weak scaling, no collective on the data path); timing is CUDA
+events on each rank, the maximum over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "draft-tree cycles/sec (score+build+GDN verify+commit) at batch 64; % roofline"
+WORKLOAD = ("dforktree cycle: batch 64/GPU, S=24, V=248320 fp32 logits, 2M+8M n-gram table, B=32 nodes, M=16, "
+            "24 Qwen3.5-9B GDN layers (tree conv + verify, Hk=16 Hv=32 D=128, bf16 activations, fp32 state), "
+            "greedy accept (len U[1,24]), in-place commit")
+S, V, N, M, LAYERS, HK, HV, D = 24, 248320, 32, 16, 24, 16, 32, 128
+C_CONV = 2 * HK * D + HV * D
+# algorithmic bytes per unit (per layer-request), see DESIGN.md
+VERIFY_BYTES = 2 * 1024 * 1024 + 262144 + 262144 + 8192 + 262144      # S0 + q,k + v + g,beta + o
+COMMIT_BYTES_FIXED = 4 * 1024 * 1024                                   # read S0 + write S
+COMMIT_BYTES_PER_NODE = 32 * 1024                                      # k, vn rows of 32 heads
+SCORE_BYTES = S * V * 4 + 105984 * 12 + 2944                           # logits + table probes + prev/pn
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# --------------------------------------------------------- CPU baseline ----
+def _cpu_job_build(args):
+    """Oracle score+build for one request (worker process)."""
+    import numpy as np
+    from oracle import builder as OB
+    from oracle import ngram as ON
+    tdir, seed = args
+    table = {k[:-4]: np.load(os.path.join(tdir, k), mmap_mode="r") for k in os.listdir(tdir) if k.endswith(".npy")}
+    ng = ON.NGramOracle(table, beta3=60.0)
+    from dforktree_b200 import synth
+    logits = synth.make_logits(S, V, seed=seed)
+    t = time.perf_counter()
+    OB.builder_run(logits, 5, 7, ng, N=N)
+    return time.perf_counter() - t
+
+
+def _cpu_job_layer(seed):
+    """Oracle tree conv + GDN verify + commit for one layer-request."""
+    import numpy as np
+    from dforktree_b200 import synth
+    from oracle import builder as OB
+    from oracle import gdn as OG
+    d = synth.make_gdn_inputs(N, HK, HV, D, seed=seed)
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((N, C_CONV)).astype(np.float32)
+    cs = rng.standard_normal((C_CONV, 3)).astype(np.float32)
+    w = rng.standard_normal((C_CONV, 4)).astype(np.float32)
+    t = time.perf_counter()
+    _, _, cidx = OB.tree_struct(d["parent"], 4)
+    OG.tree_conv(x, cs, w, None, cidx)
+    o, k, vn, G = OG.tree_gdn(d["y"], d["a"], d["b"], d["A_log"], d["dt_bias"], d["pool"], 0, d["anc"], HK, HV, D, D)
+    u = int(d["path"][-1])
+    for h in range(HV):
+        OG.snapshot(d["pool"][0, h], k[h], vn[h], G[h], d["anc"], d["path"], u)
+    return time.perf_counter() - t
+
+
+class CpuSampler:
+    """The oracle port timed on the host cores for the bench workload: a spawn
+    pool of `workers` single-threaded processes sharing the n-gram table
+    (memory-mapped), warmed once; `rate()` runs a bounded sample and scales it
+    to one batch-64 cycle."""
+
+    def __init__(self, workers: int):
+        import multiprocessing as mp
+
+        import numpy as np
+
+        from dforktree_b200 import synth
+        self.workers = workers
+        table = synth.make_ngram_table(V, 2_000_000, 8_000_000, seed=0)
+        self.tdir = tempfile.mkdtemp(prefix="dft_table_")
+        for k, v in table.items():
+            np.save(os.path.join(self.tdir, k + ".npy"), np.asarray(v))
+        self._env = {k: os.environ.get(k) for k in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")}
+        for k in self._env:
+            os.environ[k] = "1"
+        self.pool = mp.get_context("spawn").Pool(workers)
+        self.pool.map(_cpu_job_layer, [10_000 + i for i in range(workers)])
+        self.pool.map(_cpu_job_build, [(self.tdir, 10_000 + i) for i in range(workers)])
+
+    def rate(self, builds_per_worker: int = 1, layers_per_worker: int = 2, seed: int = 0):
+        w = self.workers
+        tb = self.pool.map(_cpu_job_build, [(self.tdir, seed * 1000 + i) for i in range(w * builds_per_worker)])
+        tl = self.pool.map(_cpu_job_layer, [seed * 1000 + i for i in range(w * layers_per_worker)])
+        # concurrent workers: throughput = units / (total compute time / workers)
+        rate_b = len(tb) / (sum(tb) / w)
+        rate_l = len(tl) / (sum(tl) / w)
+        cycle_s = 64 / rate_b + 64 * LAYERS / rate_l
+        sample = (f"{len(tb)} request score+builds and {len(tl)} layer-request conv+verify+commits "
+                  f"(of 64 and {64 * LAYERS} per cycle) on {w} single-threaded processes, scaled to one cycle")
+        return 1.0 / cycle_s, sample, dict(build_s=sum(tb) / len(tb), layer_s=sum(tl) / len(tl))
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+        for k, v in self._env.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+        for f in os.listdir(self.tdir):
+            os.unlink(os.path.join(self.tdir, f))
+        os.rmdir(self.tdir)
+
+
+# ------------------------------------------------------------- clocks ------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        try:
+            rows = [r.split(",") for r in open(self.path).read().strip().split("\n") if r.strip()]
+            os.unlink(self.path)
+        except Exception:
+            return None
+        rows = [[x.strip() for x in r] for r in rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- ours -----
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from dforktree_b200 import build as B
+    from dforktree_b200 import kernels as K
+    from dforktree_b200 import synth
+    from dforktree_b200.cycle import CycleConfig, DraftTreeCycle
+
+    if rank == 0:
+        B.build()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = CycleConfig(B=args.batch, layers=args.layers)
+    table_np = synth.make_ngram_table(V, 2_000_000, 8_000_000, seed=0)
+    from dforktree_b200.ngram_gpu import load_npz_arrays
+    table = K.Table(load_npz_arrays(table_np), beta3=60.0, device=dev)
+    cyc = DraftTreeCycle(cfg, table, dev, seed=rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    Bt = cfg.B
+    # synthetic per-step inputs, resident in HBM (larger than L2: no flush needed)
+    logits = torch.randn(Bt, S, V, device=dev, generator=g) * 3.0
+    pk = torch.randint(0, V, (Bt, S), device=dev, generator=g)
+    logits.view(-1, V)[torch.arange(Bt * S, device=dev), pk.view(-1)] += 6.0
+    root = torch.randint(0, V, (Bt,), device=dev, generator=g)
+    pre1 = torch.randint(0, V, (Bt,), device=dev, generator=g)
+    x = torch.randn(cfg.layers, Bt, N, cfg.C, device=dev, generator=g).to(torch.bfloat16)
+    a = torch.randn(cfg.layers, Bt, N, HV, device=dev, generator=g).to(torch.bfloat16)
+    b = torch.randn(cfg.layers, Bt, N, HV, device=dev, generator=g).to(torch.bfloat16)
+    acc_len = torch.randint(1, 25, (Bt,), device=dev, generator=g)
+
+    def target_fn(tree):
+        # target model stand-in: agrees with the first-child chain up to the drawn length
+        nx = tree["nxt"]
+        tgt = torch.gather(tree["tokens"], 1, nx.clamp(min=0))
+        keep = (nx >= 0) & (tree["depth"] + 1 < acc_len[:, None])
+        return torch.where(keep, tgt, torch.full_like(tgt, -1))
+
+    stream = torch.cuda.current_stream(dev)
+
+    def one_step(ev=None):
+        if ev is None:
+            cyc.step(logits, root, pre1, x, a, b, target_fn)
+            return
+        ev["sb0"].record(stream)
+        cyc.build(logits, root, pre1)
+        ev["sb1"].record(stream)
+        for l in range(cfg.layers):
+            cyc.verify_layer(l, x[l], a[l], b[l])
+        ev["v1"].record(stream)
+        cyc.accept(target_fn(cyc.tree))
+        ev["c0"].record(stream)
+        cyc.commit()
+        ev["c1"].record(stream)
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    # per-stage events on a separate pass of K steps (same work)
+    mk = lambda: torch.cuda.Event(enable_timing=True)
+    stage = {"score_build": 0.0, "conv_verify": 0.0, "accept": 0.0, "commit": 0.0}
+    evs = []
+    for _ in range(args.steps):
+        ev = {k: mk() for k in ("sb0", "sb1", "v1", "c0", "c1")}
+        one_step(ev)
+        evs.append(ev)
+    torch.cuda.synchronize()
+    for ev in evs:
+        stage["score_build"] += ev["sb0"].elapsed_time(ev["sb1"])
+        stage["conv_verify"] += ev["sb1"].elapsed_time(ev["v1"])
+        stage["accept"] += ev["v1"].elapsed_time(ev["c0"])
+        stage["commit"] += ev["c0"].elapsed_time(ev["c1"])
+    # per-launch verify duration: conv and verify timed separately on one pass
+    conv_ms = verify_ms = 0.0
+    pairs = []
+    for _ in range(args.steps):
+        cyc.build(logits, root, pre1)
+        for l in range(cfg.layers):
+            e0, e1, e2 = mk(), mk(), mk()
+            c = cyc.cfg
+            e0.record(stream)
+            K.tree_conv(x[l], cyc.conv_state[l], cyc.conv_w[l], None, cyc.tree["cidx"], y=cyc.y)
+            e1.record(stream)
+            K.gdn_tree_verify(cyc.y, a[l], b[l], None, cyc.dt_bias[l], cyc.tree["anc"], cyc.pool[l], c.Hk, c.Hv,
+                              c.D, c.D, neg_exp_A=cyc.neg_exp_A[l], o=cyc.o, aux_k=cyc.aux_k[l],
+                              aux_vn=cyc.aux_vn[l], aux_g=cyc.aux_g[l], aux_k_per_v=False)
+            e2.record(stream)
+            pairs.append((e0, e1, e2))
+        cyc.accept(target_fn(cyc.tree))
+        cyc.commit()
+    torch.cuda.synchronize()
+    for e0, e1, e2 in pairs:
+        conv_ms += e0.elapsed_time(e1)
+        verify_ms += e1.elapsed_time(e2)
+    n_verify = len(pairs)
+
+    # ---- timed region: exactly K steps, barrier + sync on both sides
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = mk(), mk()
+    with ClockSampler(local_rank) as clk:
+        t0.record(stream)
+        for _ in range(args.steps):
+            one_step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    mean_acc = float(cyc.accept_len.float().mean())
+    ms_max = ms
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_max = float(tt)
+    value = world * args.steps / (ms_max / 1e3)
+
+    # ---- end to end through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        ke = max(1, min(args.steps, 6))
+        h_logits = torch.empty(logits.shape, dtype=logits.dtype, pin_memory=True)
+        h_x = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        h_a = torch.empty(a.shape, dtype=a.dtype, pin_memory=True)
+        h_b = torch.empty(b.shape, dtype=b.dtype, pin_memory=True)
+        h_root = torch.empty(root.shape, dtype=root.dtype, pin_memory=True)
+        h_pre1 = torch.empty(pre1.shape, dtype=pre1.dtype, pin_memory=True)
+        for h, d_ in ((h_logits, logits), (h_x, x), (h_a, a), (h_b, b), (h_root, root), (h_pre1, pre1)):
+            h.copy_(d_)
+        h_tok = torch.empty((Bt, N), dtype=torch.int64, pin_memory=True)
+        h_par = torch.empty((Bt, N), dtype=torch.int64, pin_memory=True)
+        h_len = torch.empty((Bt,), dtype=torch.int64, pin_memory=True)
+        d_logits, d_x, d_a, d_b = (torch.empty_like(t) for t in (logits, x, a, b))
+        d_root, d_pre1 = torch.empty_like(root), torch.empty_like(pre1)
+        h2d = sum(t.numel() * t.element_size() for t in (h_logits, h_x, h_a, h_b, h_root, h_pre1))
+        d2h = sum(t.numel() * t.element_size() for t in (h_tok, h_par, h_len))
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s0, s1 = mk(), mk()
+        s0.record(stream)
+        for _ in range(ke):
+            for d_, h in ((d_logits, h_logits), (d_x, h_x), (d_a, h_a), (d_b, h_b), (d_root, h_root),
+                          (d_pre1, h_pre1)):
+                d_.copy_(h, non_blocking=True)
+            cyc.step(d_logits, d_root, d_pre1, d_x, d_a, d_b, target_fn)
+            h_tok.copy_(cyc.tree["tokens"], non_blocking=True)
+            h_par.copy_(cyc.tree["parent"], non_blocking=True)
+            h_len.copy_(cyc.accept_len, non_blocking=True)
+        s1.record(stream)
+        torch.cuda.synchronize()
+        ems = s0.elapsed_time(s1)
+        if world > 1:
+            tt = torch.tensor([ems], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ems = float(tt)
+        e2e = {"value": world * ke / (ems / 1e3), "unit": "cycles/s", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "steps": ke}
+    status = int(cyc.status.item())
+
+    if rank != 0:
+        return None
+    hbm, tflops, peak_kind = _peaks()
+    verify_launch_ms = verify_ms / max(n_verify, 1)
+    commit_launch_ms = stage["commit"] / args.steps
+    verify_bytes = Bt * VERIFY_BYTES
+    commit_bytes = Bt * LAYERS * (COMMIT_BYTES_FIXED + COMMIT_BYTES_PER_NODE * mean_acc)
+    traffic = _traffic()
+    cand = {
+        "gdn_verify": (verify_launch_ms * LAYERS, verify_bytes, verify_launch_ms),
+        "gdn_commit": (commit_launch_ms, commit_bytes, commit_launch_ms),
+    }
+    dom = max(cand, key=lambda k: cand[k][0])
+    _, nbytes, lms = cand[dom]
+    achieved = nbytes / (lms / 1e3) / 1e9
+    roof = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
+            "algorithmic_bytes_per_launch": int(nbytes), "launch_ms": round(lms, 4),
+            "traffic": traffic.get(dom)}
+    per_kernel = {
+        "score_build_ms": stage["score_build"] / args.steps,
+        "tree_conv_ms_per_layer": conv_ms / max(n_verify, 1),
+        "gdn_verify_ms_per_layer": verify_launch_ms,
+        "accept_ms": stage["accept"] / args.steps,
+        "gdn_commit_ms": commit_launch_ms,
+        "score_build_GBps": Bt * SCORE_BYTES / (stage["score_build"] / args.steps / 1e3) / 1e9,
+        "gdn_verify_GBps": verify_bytes / (verify_launch_ms / 1e3) / 1e9,
+        "gdn_commit_GBps": commit_bytes / (commit_launch_ms / 1e3) / 1e9,
+        "mean_accept_len": mean_acc,
+    }
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "cycles/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch_per_gpu": Bt, "S": S, "V": V, "N": N, "M": M, "layers": cfg.layers,
+                   "Hk": HK, "Hv": HV, "D": D, "parallelism": f"request-sharded x{world}",
+                   "l2": "inputs larger than L2 (logits 1.5 GB, states 3 GiB per GPU); no flush"},
+        "roofline": roof, "stages": {k: round(v, 4) for k, v in per_kernel.items()},
+        "gpu_launches": cyc.launches_per_step * args.steps, "dev_status": status,
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    line["clocks"] = clk.summary()
+    return line
+
+
+def _traffic():
+    """DRAM bytes per launch of the bench kernels from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ----------------------------------------------------------- reference -----
+def run_reference(args):
+    rates = []
+    workers = max(1, min(os.cpu_count() or 1, 64))
+    sampler = CpuSampler(workers)
+    try:
+        for step in range(args.warmup + args.steps):
+            r, sample, _ = sampler.rate(1, 2, seed=step)
+            if step >= args.warmup:
+                rates.append(r)
+    finally:
+        sampler.close()
+    v = statistics.median(rates)
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": "cycles/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": 64},
+            "cpu_baseline": {"value": v, "unit": "cycles/s", "cores": workers, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "cycles/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # before the first GPU call (spawned workers)
+        workers = max(1, min(os.cpu_count() or 1, 64))
+        sampler = CpuSampler(workers)
+        try:
+            v, sample, _ = sampler.rate(2, 4)
+        finally:
+            sampler.close()
+        cpu = {"value": v, "unit": "cycles/s", "cores": workers, "kind": "port", "sample": sample}
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    line = run_ours(args, rank, world, local_rank)
+    if line is not None:
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,153 @@
+// Closed-form commit of the accepted path's recurrent state.
+// Reference: fc1_fused.snapshots (fc1_fused.py:27-49): for each layer, head
+// and end node u,
+//   S_u = e^{G_u} S0 + sum_{t in path, t anc-or-self of u} e^{G_u - G_t} k_t vn_t^T
+// written to the intermediate state buffer (in place into the pool when the
+// caller asks).  One CTA per (end, layer, request, v-head) streams the
+// 64 KiB fp32 state tile once in and once out with 128-bit accesses (all
+// sixteen loads of a thread in flight before the FMAs); the <= 64 path rows
+// of k and e^{G_u-G_t} vn sit in shared memory.  fp32 FMA on CUDA cores: at
+// L = 24 the tile needs ~6 FLOP/B, below the CUDA-core ridge on B200.
+#include "dft_common.cuh"
+
+using namespace dft;
+
+namespace {
+
+constexpr int kD = 128;
+constexpr int kThreads = 256;
+constexpr int kMaxPath = 64;
+
+__global__ void __launch_bounds__(kThreads) gdn_commit_kernel(dft_commit_args a, int32_t* st) {
+  extern __shared__ __align__(16) float s_path[];  // [cap][kD] k*w, then [cap][kD] vn
+  __shared__ int s_ids[kMaxPath];
+  __shared__ float s_w[kMaxPath];
+  __shared__ int s_n;
+
+  // blockIdx.x = ((e * L + l) * B + b) * Hv + h
+  int bid = blockIdx.x;
+  const int h = bid % a.Hv;
+  bid /= a.Hv;
+  const int b = bid % a.B;
+  bid /= a.B;
+  const int l = bid % a.L;
+  const int e = bid / a.L;
+  const int tid = threadIdx.x;
+  const int64_t u = a.ends[(int64_t)b * a.E + e];
+  if (u < 0) return;  // fc1_fused.py:49 store masked by u >= 0
+  if (u >= a.N) {
+    if (tid == 0) raise_status(st, DFT_DEV_BAD_INDEX);
+    return;
+  }
+  const int R = a.Hv / a.Hk;
+  const int khead = a.aux_k_per_v ? h : h / R;
+  const float* G = a.aux_g + (int64_t)l * a.ag_sl + (int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh;
+  const float gu = G[u];
+  if (tid == 0) {
+    // path nodes that are ancestors-or-self of u, in path order (fc1_fused.py:30-35)
+    int n = 0;
+    const float* anc_u = a.anc + ((int64_t)b * a.N + u) * a.N;
+    for (int t = 0; t < a.P; ++t) {
+      const int64_t id = a.path[(int64_t)b * a.P + t];
+      if (id < 0) continue;
+      if (id >= a.N) {
+        raise_status(st, DFT_DEV_BAD_INDEX);
+        continue;
+      }
+      if (anc_u[id] > 0.f && n < a.P && n < a.N) {
+        s_ids[n] = (int)id;
+        s_w[n] = expf(gu - G[id]);
+        ++n;
+      }
+    }
+    s_n = n;
+  }
+  __syncthreads();
+  const int np = s_n;
+  const int cap = a.P < a.N ? a.P : a.N;
+  float (*skk)[kD] = reinterpret_cast<float (*)[kD]>(s_path);
+  float (*svv)[kD] = reinterpret_cast<float (*)[kD]>(s_path + (size_t)cap * kD);
+  const float* Kb = a.aux_k + (int64_t)l * a.ak_sl + (int64_t)b * a.ak_sb + (int64_t)khead * a.ak_sh;
+  const float* Vb = a.aux_vn + (int64_t)l * a.av_sl + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh;
+  for (int i = tid; i < np * kD; i += kThreads) {
+    const int t = i >> 7, d = i & 127;
+    const int id = s_ids[t];
+    skk[t][d] = Kb[(int64_t)id * a.ak_sn + d] * s_w[t];  // (k * w) (fc1_fused.py:39)
+    svv[t][d] = Vb[(int64_t)id * a.av_sn + d];
+  }
+  const int64_t slot = a.slots_in ? a.slots_in[b] : b;
+  const int64_t dst = a.slots_out ? a.slots_out[b] : b;
+  const float* S0 = a.state_in + (int64_t)l * a.si_sl + slot * a.si_ss + (int64_t)h * a.si_sh;
+  float* So = a.state_out + (int64_t)l * a.so_sl + dst * a.so_ss + u * a.so_su + (int64_t)h * a.so_sh;
+  const float eg = expf(gu);
+  const int k4 = (tid & 31) * 4;
+  const int v0 = tid >> 5;  // rows v0, v0 + 8, ..., 16 rows per thread
+  const bool vec = a.si_sk == 1 && a.so_sk == 1 && (a.si_sv % 4 == 0) && (a.so_sv % 4 == 0) &&
+                   ((uintptr_t)S0 % 16 == 0) && ((uintptr_t)So % 16 == 0);
+  float4 acc[16];
+  if (vec) {
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = __ldcs(reinterpret_cast<const float4*>(S0 + (int64_t)(v0 + 8 * r) * a.si_sv + k4));
+  } else {
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const float* p = S0 + (int64_t)(v0 + 8 * r) * a.si_sv + (int64_t)k4 * a.si_sk;
+      acc[r] = make_float4(p[0], p[a.si_sk], p[2 * a.si_sk], p[3 * a.si_sk]);
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    acc[r].x *= eg;
+    acc[r].y *= eg;
+    acc[r].z *= eg;
+    acc[r].w *= eg;
+  }
+  for (int t = 0; t < np; ++t) {
+    const float4 kk = *reinterpret_cast<const float4*>(&skk[t][k4]);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const float vv = svv[t][v0 + 8 * r];
+      acc[r].x = fmaf(vv, kk.x, acc[r].x);
+      acc[r].y = fmaf(vv, kk.y, acc[r].y);
+      acc[r].z = fmaf(vv, kk.z, acc[r].z);
+      acc[r].w = fmaf(vv, kk.w, acc[r].w);
+    }
+  }
+  if (vec) {
+#pragma unroll
+    for (int r = 0; r < 16; ++r) __stcs(reinterpret_cast<float4*>(So + (int64_t)(v0 + 8 * r) * a.so_sv + k4), acc[r]);
+  } else {
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float* p = So + (int64_t)(v0 + 8 * r) * a.so_sv + (int64_t)k4 * a.so_sk;
+      p[0] = acc[r].x;
+      p[a.so_sk] = acc[r].y;
+      p[2 * a.so_sk] = acc[r].z;
+      p[3 * a.so_sk] = acc[r].w;
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int dft_gdn_commit(const dft_commit_args* a, int32_t* dev_status, void* stream) {
+  if (!a || !a->state_in || !a->state_out || !a->aux_k || !a->aux_vn || !a->aux_g || !a->anc || !a->path ||
+      !a->ends)
+    return DFT_ERR_INVALID;
+  if (a->L <= 0 || a->B <= 0 || a->N <= 0 || a->Hk <= 0 || a->Hv <= 0 || a->P < 0 || a->E <= 0)
+    return DFT_ERR_INVALID;
+  if (a->Hv % a->Hk) return DFT_ERR_INVALID;
+  if (a->Dk != kD || a->Dv != kD || a->P > kMaxPath || a->N > kMaxNodes) return DFT_ERR_UNSUPPORTED;
+  const int64_t blocks = (int64_t)a->E * a->L * a->B * a->Hv;
+  if (blocks > 0x7fffffffll) return DFT_ERR_UNSUPPORTED;
+  if (a->P == 0) return DFT_ERR_UNSUPPORTED;
+  const int cap = a->P < a->N ? a->P : a->N;
+  const size_t sm = 2 * (size_t)cap * kD * sizeof(float);
+  if (sm > 48 * 1024 &&
+      cudaFuncSetAttribute(gdn_commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+    return DFT_ERR_CUDA;
+  gdn_commit_kernel<<<(unsigned)blocks, kThreads, sm, reinterpret_cast<cudaStream_t>(stream)>>>(*a, dev_status);
+  DFT_LAUNCH_CHECK();
+  return DFT_OK;
+}

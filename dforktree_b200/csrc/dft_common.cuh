@@ -1,0 +1,177 @@
+// Shared device helpers for the dforktree_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/dforktree_b200.h"
+
+#define DFT_CUDA_CHECK(expr)                                   \
+  do {                                                         \
+    cudaError_t _e = (expr);                                   \
+    if (_e != cudaSuccess) return DFT_ERR_CUDA;                \
+  } while (0)
+
+#define DFT_LAUNCH_CHECK() DFT_CUDA_CHECK(cudaGetLastError())
+
+namespace dft {
+
+constexpr unsigned long long kEmptyKey = 0xFFFFFFFFFFFFFFFFull;
+constexpr int kMaxNodes = 64;
+
+// ---------------------------------------------------------------- dtypes --
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+__device__ __forceinline__ float load_any(const void* p, int dtype, int64_t i) {
+  switch (dtype) {
+    case DFT_BF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    case DFT_F16: return __half2float(reinterpret_cast<const __half*>(p)[i]);
+    default: return reinterpret_cast<const float*>(p)[i];
+  }
+}
+__device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v) {
+  switch (dtype) {
+    case DFT_BF16: reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v); break;
+    case DFT_F16: reinterpret_cast<__half*>(p)[i] = __float2half_rn(v); break;
+    default: reinterpret_cast<float*>(p)[i] = v;
+  }
+}
+
+inline bool valid_dtype(int d) { return d == DFT_F32 || d == DFT_BF16 || d == DFT_F16; }
+
+// ------------------------------------------------------------ status word --
+__device__ __forceinline__ void raise_status(int32_t* st, int bits) {
+  if (st) atomicOr(st, bits);
+}
+
+// ------------------------------------------------------------------ hash --
+// 64-bit finaliser (xor-shift-multiply), well mixed in the low bits.
+__host__ __device__ __forceinline__ unsigned long long mix64(unsigned long long x) {
+  x ^= x >> 33;
+  x *= 0xff51afd7ed558ccdull;
+  x ^= x >> 33;
+  x *= 0xc4ceb9fe1a85ec53ull;
+  x ^= x >> 33;
+  return x;
+}
+
+// One 16-byte hash slot: 64-bit key + two 32-bit payload words.
+struct __align__(16) Slot {
+  unsigned long long key;
+  float f0;      // pair: bigram count   | triple: c3     | quad: c4
+  uint32_t u1;   // pair: n3c (as float) | triple: rank3  | quad: unused
+};
+
+__device__ __forceinline__ uint4 ldg_slot(const Slot* s) {
+  return __ldg(reinterpret_cast<const uint4*>(s));
+}
+__device__ __forceinline__ unsigned long long slot_key(uint4 v) {
+  return (static_cast<unsigned long long>(v.y) << 32) | v.x;
+}
+
+// Device view of the n-gram tables (POD, passed by value).
+struct TableView {
+  int64_t V;
+  const Slot* pair; unsigned long long pair_mask;
+  const Slot* trip; unsigned long long trip_mask;
+  const Slot* quad; unsigned long long quad_mask;
+  const float* prev;
+  const float* pn;
+  const float* n4c;
+  int has_pair, has_trip, has_quad, has_ctx;
+  float beta2, beta3, beta4, clip;
+};
+
+// Probe an open-addressed table; returns the matching slot (key == q) or a
+// zero slot on a miss.  Negative keys never match (table keys are >= 0).
+__device__ __forceinline__ uint4 probe(const Slot* tab, unsigned long long mask, long long q,
+                                       int32_t* status) {
+  uint4 z = make_uint4(0, 0, 0, 0);
+  if (q < 0 || tab == nullptr) return z;
+  unsigned long long uq = static_cast<unsigned long long>(q);
+  unsigned long long h = mix64(uq) & mask;
+  for (unsigned long long n = 0; n <= mask; ++n) {
+    uint4 s = ldg_slot(tab + h);
+    unsigned long long k = slot_key(s);
+    if (k == uq) return s;
+    if (k == kEmptyKey) return z;
+    h = (h + 1) & mask;
+  }
+  raise_status(status, DFT_DEV_PROBE_LIMIT);
+  return z;
+}
+
+// Continue probing after a first slot `s0` was loaded from bucket mix64(q)&mask.
+__device__ __forceinline__ uint4 probe_from(const Slot* tab, unsigned long long mask, long long q, uint4 s0,
+                                            int32_t* status) {
+  uint4 z = make_uint4(0, 0, 0, 0);
+  if (q < 0 || tab == nullptr) return z;
+  unsigned long long uq = static_cast<unsigned long long>(q);
+  unsigned long long k = slot_key(s0);
+  if (k == uq) return s0;
+  if (k == kEmptyKey) return z;
+  unsigned long long h = (mix64(uq) + 1) & mask;
+  for (unsigned long long n = 1; n <= mask; ++n) {
+    uint4 s = ldg_slot(tab + h);
+    k = slot_key(s);
+    if (k == uq) return s;
+    if (k == kEmptyKey) return z;
+    h = (h + 1) & mask;
+  }
+  raise_status(status, DFT_DEV_PROBE_LIMIT);
+  return z;
+}
+
+__device__ __forceinline__ uint4 first_slot(const Slot* tab, unsigned long long mask, long long q) {
+  if (q < 0 || tab == nullptr) return make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0, 0);
+  return ldg_slot(tab + (mix64(static_cast<unsigned long long>(q)) & mask));
+}
+
+// torch-style wrap of a negative index into pn[] (ngram_gpu.py:42,70 index
+// pn[c] with torch semantics); ids outside [-V, V) flag DFT_DEV_BAD_TOKEN.
+__device__ __forceinline__ float pn_at(const TableView& t, long long c, int32_t* status) {
+  if (c < 0) c += t.V;
+  if (c < 0 || c >= t.V) {
+    raise_status(status, DFT_DEV_BAD_TOKEN);
+    return 1.0f;
+  }
+  return __ldg(t.pn + c);
+}
+
+// p2(b, c) = (n_bc + beta2 * pn[c]) / (prev[b] + beta2)   (ngram_gpu.py:39-42)
+// The multiply and the adds are separate float32 roundings, as in torch.
+__device__ __forceinline__ float p2_from(float n_bc, float prev_b, float pn_c, float beta2) {
+  return __fdiv_rn(__fadd_rn(n_bc, __fmul_rn(beta2, pn_c)), __fadd_rn(prev_b, beta2));
+}
+// p3 = (n_abc + beta3 * p2) / (n_ab + beta3)               (ngram_gpu.py:44-51)
+__device__ __forceinline__ float p3_from(float n_abc, float n_ab, float p2, float beta3) {
+  return __fdiv_rn(__fadd_rn(n_abc, __fmul_rn(beta3, p2)), __fadd_rn(n_ab, beta3));
+}
+// pmi = clamp(log p - log pn[c], -clip, clip)               (ngram_gpu.py:70)
+__device__ __forceinline__ float pmi_from(float p, float log_pn, float clip) {
+  float v = __fsub_rn(logf(p), log_pn);
+  return fminf(fmaxf(v, -clip), clip);
+}
+
+// ------------------------------------------------------------ warp utils --
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace dft

@@ -1,0 +1,252 @@
+// Gated-DeltaNet tree verifier.
+//
+// Reference: tree_gdn_split (tree_kernels.py:193-208) = _tree_prepare
+// (:136-164) -> invert32 (fc1_block_inverse.py:69-78) -> _tree_finish
+// (:167-191), three launches with q/k/G/beta/X round-tripping through HBM.
+// Here one CTA per (request, v-head) does everything in shared memory.
+//
+// Algebra (per v-head, N tree nodes, S0 = state [Dk, Dv]):
+//   A  = strict-ancestor(beta_i k_i.k_j e^{G_i-G_j}),  X = (I + A)^-1
+//   vn = X(beta v) - X(beta e^G k) S0 = X R,  R = beta (v - e^G (k S0))
+//   o  = e^G (q S0) + (q k^T . D) vn = e^G (q S0) + Z R,  Z = (q k^T . D) X
+// which needs only the two S0 contractions k S0 and q S0 (the reference
+// computes Wk S0 with Wk = X(beta e^G k) instead; same result).
+// This file holds the SIMT (CUDA-core fp32) implementation.
+#include "dft_common.cuh"
+
+using namespace dft;
+
+namespace {
+
+constexpr int kD = 128;        // Dk = Dv = 128 (Qwen3.5 GDN)
+constexpr int kLD = kD + 1;    // padded row of the state tile (column reads)
+constexpr int kThreads = 256;
+
+template <int BN>
+struct GdnSmem {
+  static constexpr size_t q = 0;
+  static constexpr size_t k = q + sizeof(float) * BN * kD;
+  static constexpr size_t v = k + sizeof(float) * BN * kD;
+  static constexpr size_t P = v + sizeof(float) * BN * kD;
+  static constexpr size_t m1 = P + sizeof(float) * kD * kLD;
+  static constexpr size_t m2 = m1 + sizeof(float) * BN * BN;
+  static constexpr size_t mx = m2 + sizeof(float) * BN * BN;
+  static constexpr size_t total = mx + sizeof(float) * BN * BN;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads) gdn_verify_simt(dft_gdn_args a, int32_t* st) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  using L = GdnSmem<BN>;
+  float* sq = (float*)(smem + L::q);
+  float* sk = (float*)(smem + L::k);
+  float* sv = (float*)(smem + L::v);
+  float* sP = (float*)(smem + L::P);
+  float* m1 = (float*)(smem + L::m1);  // k k^T -> A -> Z
+  float* m2 = (float*)(smem + L::m2);  // q k^T -> PD
+  float* mX = (float*)(smem + L::mx);  // X
+  __shared__ float sg[BN], sbeta[BN], sG[BN], seG[BN];
+  __shared__ unsigned long long sanc[BN];
+
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int N = a.N, R = a.Hv / a.Hk, hk = h / R;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float scale = a.scale;
+  const int64_t ybase = (int64_t)b * a.y_sb;
+  const int KD = a.Hk * kD;
+
+  // ---- phase 0: q, k rows (L2-normalised), v rows, gates, state tile
+  for (int n = warp; n < BN; n += kThreads / 32) {
+    float4 qv = make_float4(0.f, 0.f, 0.f, 0.f), kv = qv, vv = qv;
+    if (n < N) {
+      const int64_t r = ybase + (int64_t)n * a.y_sn;
+      const int d = lane * 4;
+      qv = make_float4(load_any(a.y, a.y_dtype, r + hk * kD + d), load_any(a.y, a.y_dtype, r + hk * kD + d + 1),
+                       load_any(a.y, a.y_dtype, r + hk * kD + d + 2), load_any(a.y, a.y_dtype, r + hk * kD + d + 3));
+      kv = make_float4(load_any(a.y, a.y_dtype, r + KD + hk * kD + d),
+                       load_any(a.y, a.y_dtype, r + KD + hk * kD + d + 1),
+                       load_any(a.y, a.y_dtype, r + KD + hk * kD + d + 2),
+                       load_any(a.y, a.y_dtype, r + KD + hk * kD + d + 3));
+      vv = make_float4(load_any(a.y, a.y_dtype, r + 2 * KD + h * kD + d),
+                       load_any(a.y, a.y_dtype, r + 2 * KD + h * kD + d + 1),
+                       load_any(a.y, a.y_dtype, r + 2 * KD + h * kD + d + 2),
+                       load_any(a.y, a.y_dtype, r + 2 * KD + h * kD + d + 3));
+      // tree_kernels.py:144-145: x * rsqrt(sum x^2 + 1e-6) (* scale for q)
+      const float rq = 1.f / sqrtf(warp_sum(qv.x * qv.x + qv.y * qv.y + qv.z * qv.z + qv.w * qv.w) + 1e-6f);
+      const float rk = 1.f / sqrtf(warp_sum(kv.x * kv.x + kv.y * kv.y + kv.z * kv.z + kv.w * kv.w) + 1e-6f);
+      qv = make_float4(qv.x * rq * scale, qv.y * rq * scale, qv.z * rq * scale, qv.w * rq * scale);
+      kv = make_float4(kv.x * rk, kv.y * rk, kv.z * rk, kv.w * rk);
+      if (a.aux_k && (a.aux_k_per_v || h % R == 0)) {
+        float* dstk = a.aux_k + (int64_t)b * a.ak_sb + (int64_t)(a.aux_k_per_v ? h : hk) * a.ak_sh +
+                      (int64_t)n * a.ak_sn + d;
+        *reinterpret_cast<float4*>(dstk) = kv;
+      }
+    }
+    *reinterpret_cast<float4*>(sq + n * kD + lane * 4) = qv;
+    *reinterpret_cast<float4*>(sk + n * kD + lane * 4) = kv;
+    *reinterpret_cast<float4*>(sv + n * kD + lane * 4) = vv;
+  }
+  {
+    int64_t slot = a.state_slots ? a.state_slots[b] : b;
+    if (slot < 0) slot = 0;  // tree_kernels.py:184 max(slot, 0)
+    const float* P = a.pool + slot * a.p_ss + (int64_t)h * a.p_sh;
+    for (int e = tid; e < kD * kD; e += kThreads) {
+      const int vrow = e >> 7, kcol = e & 127;
+      sP[vrow * kLD + kcol] = __ldg(P + vrow * a.p_sv + kcol * a.p_sk);
+    }
+  }
+  if (tid < BN) {
+    const int n = tid;
+    float g = 0.f, beta = 0.f;
+    unsigned long long m = 0ull;
+    if (n < N) {
+      const int64_t ab = (int64_t)b * a.ab_sb + (int64_t)n * a.ab_sn + h;
+      const float ar = load_any(a.a, a.ab_dtype, ab) + load_any(a.dt_bias, a.dtb_dtype, h);
+      const float sp = ar > 20.f ? ar : logf(1.f + expf(fminf(ar, 20.f)));
+      const float dec = a.neg_exp_A ? a.neg_exp_A[h] : -expf(a.A_log[h]);
+      g = dec * sp;
+      beta = 1.f / (1.f + expf(-load_any(a.bg, a.ab_dtype, ab)));
+      const float* ar_anc = a.anc + ((int64_t)b * N + n) * N;
+      for (int j = 0; j < N; ++j)
+        if (ar_anc[j] > 0.5f) m |= 1ull << j;
+    }
+    sg[n] = g;
+    sbeta[n] = beta;
+    sanc[n] = m;
+  }
+  __syncthreads();
+
+  // ---- phase 1: G = Anc g (tree_kernels.py:153), k k^T and q k^T
+  if (tid < BN) {
+    float G = 0.f;
+    const unsigned long long m = sanc[tid];
+    for (int j = 0; j < N; ++j)
+      if ((m >> j) & 1ull) G += sg[j];
+    sG[tid] = G;
+    seG[tid] = expf(G);
+  }
+  for (int i = warp; i < N; i += kThreads / 32) {
+    const float4 qi = *reinterpret_cast<const float4*>(sq + i * kD + lane * 4);
+    const float4 ki = *reinterpret_cast<const float4*>(sk + i * kD + lane * 4);
+    for (int j = 0; j < N; ++j) {
+      const float4 kj = *reinterpret_cast<const float4*>(sk + j * kD + lane * 4);
+      float pk = ki.x * kj.x + ki.y * kj.y + ki.z * kj.z + ki.w * kj.w;
+      float pq = qi.x * kj.x + qi.y * kj.y + qi.z * kj.z + qi.w * kj.w;
+      pk = warp_sum(pk);
+      pq = warp_sum(pq);
+      if (lane == 0) {
+        m1[i * BN + j] = pk;
+        m2[i * BN + j] = pq;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 2: A (strict ancestors) and PD = (q k^T) . D
+  for (int e = tid; e < N * N; e += kThreads) {
+    const int i = e / N, j = e % N;
+    const bool anc = (sanc[i] >> j) & 1ull;
+    const float D = anc ? expf(sG[i] - sG[j]) : 0.f;
+    m1[i * BN + j] = (anc && i != j) ? sbeta[i] * m1[i * BN + j] * D : 0.f;
+    m2[i * BN + j] = anc ? m2[i * BN + j] * D : 0.f;
+  }
+  __syncthreads();
+
+  // ---- phase 3: X = (I + A)^-1 by forward substitution, one column per thread
+  if (tid < N) {
+    const int c = tid;
+    for (int i = 0; i < N; ++i) {
+      float x = (i == c) ? 1.f : 0.f;
+      if (i > c) {
+        for (int m = c; m < i; ++m) x -= m1[i * BN + m] * mX[m * BN + c];
+      }
+      mX[i * BN + c] = x;
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 4: Z = PD X (into m1)
+  for (int e = tid; e < N * N; e += kThreads) {
+    const int n = e / N, m = e % N;
+    float z = 0.f;
+    for (int j = m; j <= n; ++j) z += m2[n * BN + j] * mX[j * BN + m];
+    m1[n * BN + m] = z;
+  }
+  // ---- phase 5: k S0 and q S0 for this thread's column v and half of the rows
+  constexpr int HR = BN / 2;
+  const int v = tid & 127, n0 = (tid >> 7) * HR;
+  float ks[HR], qs[HR];
+#pragma unroll
+  for (int r = 0; r < HR; ++r) ks[r] = qs[r] = 0.f;
+  for (int k4 = 0; k4 < kD; k4 += 4) {
+    const float p0 = sP[v * kLD + k4], p1 = sP[v * kLD + k4 + 1], p2 = sP[v * kLD + k4 + 2],
+                p3 = sP[v * kLD + k4 + 3];
+#pragma unroll
+    for (int r = 0; r < HR; ++r) {
+      const float4 kf = *reinterpret_cast<const float4*>(sk + (n0 + r) * kD + k4);
+      const float4 qf = *reinterpret_cast<const float4*>(sq + (n0 + r) * kD + k4);
+      ks[r] += kf.x * p0 + kf.y * p1 + kf.z * p2 + kf.w * p3;
+      qs[r] += qf.x * p0 + qf.y * p1 + qf.z * p2 + qf.w * p3;
+    }
+  }
+  __syncthreads();  // Z complete; all reads of sv (v rows) below are own-column
+#pragma unroll
+  for (int r = 0; r < HR; ++r) {
+    const int n = n0 + r;
+    sv[n * kD + v] = sbeta[n] * (sv[n * kD + v] - seG[n] * ks[r]);  // R
+  }
+  __syncthreads();
+
+  // ---- phase 6: vn = X R, o = e^G (q S0) + Z R
+  const int64_t obase = (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + v;
+#pragma unroll
+  for (int r = 0; r < HR; ++r) {
+    const int n = n0 + r;
+    if (n >= N) break;
+    float vn = 0.f, zr = 0.f;
+    for (int m = 0; m <= n; ++m) {
+      const float rm = sv[m * kD + v];
+      vn += mX[n * BN + m] * rm;
+      zr += m1[n * BN + m] * rm;
+    }
+    store_any(a.o, a.o_dtype, obase + (int64_t)n * a.o_sn, seG[n] * qs[r] + zr);
+    if (a.aux_vn) a.aux_vn[(int64_t)b * a.av_sb + (int64_t)h * a.av_sh + (int64_t)n * a.av_sn + v] = vn;
+  }
+  if (a.aux_g && tid < N) a.aux_g[(int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh + tid] = sG[tid];
+}
+
+template <int BN>
+int launch_simt(const dft_gdn_args& a, int32_t* st, cudaStream_t s) {
+  const size_t sm = GdnSmem<BN>::total;
+  if (cudaFuncSetAttribute(gdn_verify_simt<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+    return DFT_ERR_CUDA;
+  gdn_verify_simt<BN><<<dim3(a.Hv, a.B), kThreads, sm, s>>>(a, st);
+  DFT_LAUNCH_CHECK();
+  return DFT_OK;
+}
+
+}  // namespace
+
+int dft_gdn_check(const dft_gdn_args* a) {
+  if (!a || !a->y || !a->a || !a->bg || !a->dt_bias || !a->anc || !a->pool || !a->o) return DFT_ERR_INVALID;
+  if (!a->A_log && !a->neg_exp_A) return DFT_ERR_INVALID;
+  if (a->B <= 0 || a->B > 65535 || a->N < 1 || a->Hk <= 0 || a->Hv <= 0) return DFT_ERR_INVALID;
+  if (a->Hv % a->Hk) return DFT_ERR_INVALID;
+  if (a->Dk != kD || a->Dv != kD || a->N > kMaxNodes) return DFT_ERR_UNSUPPORTED;
+  if (!valid_dtype(a->y_dtype) || !valid_dtype(a->ab_dtype) || !valid_dtype(a->dtb_dtype) ||
+      !valid_dtype(a->o_dtype))
+    return DFT_ERR_INVALID;
+  if (a->aux_k && (a->ak_sn % 4 || a->ak_sb % 4 || a->ak_sh % 4 || ((uintptr_t)a->aux_k & 15)))
+    return DFT_ERR_INVALID;
+  return DFT_OK;
+}
+
+extern "C" int dft_gdn_tree_verify(const dft_gdn_args* args, int32_t* dev_status, void* stream) {
+  int rc = dft_gdn_check(args);
+  if (rc) return rc;
+  dft_gdn_args a = *args;
+  if (a.scale == 0.f) a.scale = 1.f / sqrtf((float)a.Dk);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (a.N <= 32) return launch_simt<32>(a, dev_status, s);
+  return launch_simt<64>(a, dev_status, s);
+}

@@ -1,0 +1,258 @@
+// Drafter-logit scoring (SURVEY row A5, fc1_builder.py:27-28):
+//   lp, ids = topk(log_softmax(logits), M);  rest = log(clamp(1 - sum exp(lp), 1e-6, 1))
+// One CTA streams one [V] row once from HBM (128-bit loads, 4 in flight per
+// thread), keeping per lane an online (max, sum-exp) pair and per warp a
+// top-16 list distributed over lanes 0..15.  A lane offers a value to the
+// warp list only when it beats the list's current 16th entry, so after the
+// first few hundred elements almost every element costs one compare.
+// Order: values descending, equal values by ascending vocabulary index.
+#include "dft_common.cuh"
+
+#include <cfloat>
+
+using namespace dft;
+
+namespace {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTopM = 16;
+
+struct TopList {
+  float v;   // lanes 0..15: sorted descending
+  int i;
+  float thr;  // value of entry 15 (warp-uniform)
+  int thr_i;
+};
+
+__device__ __forceinline__ bool before(float va, int ia, float vb, int ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+// Insert (val, idx) into the warp's list; warp-uniform call.
+__device__ __forceinline__ void list_insert(TopList& L, float val, int idx, int lane) {
+  if (!before(val, idx, L.thr, L.thr_i)) return;
+  bool ahead = lane < kTopM && before(L.v, L.i, val, idx);
+  int pos = __popc(__ballot_sync(0xffffffffu, ahead));
+  float up_v = __shfl_up_sync(0xffffffffu, L.v, 1);
+  int up_i = __shfl_up_sync(0xffffffffu, L.i, 1);
+  if (lane < kTopM) {
+    if (lane > pos) {
+      L.v = up_v;
+      L.i = up_i;
+    } else if (lane == pos) {
+      L.v = val;
+      L.i = idx;
+    }
+  }
+  L.thr = __shfl_sync(0xffffffffu, L.v, kTopM - 1);
+  L.thr_i = __shfl_sync(0xffffffffu, L.i, kTopM - 1);
+}
+
+// Offer the 4 values of every lane whose `cand` flag is set.
+__device__ __forceinline__ void offer4(TopList& L, bool cand, float4 x, int base, int lane) {
+  unsigned m = __ballot_sync(0xffffffffu, cand);
+  while (m) {
+    int src = __ffs(m) - 1;
+    m &= m - 1;
+    float a = __shfl_sync(0xffffffffu, x.x, src);
+    float b = __shfl_sync(0xffffffffu, x.y, src);
+    float c = __shfl_sync(0xffffffffu, x.z, src);
+    float d = __shfl_sync(0xffffffffu, x.w, src);
+    int bi = __shfl_sync(0xffffffffu, base, src);
+    list_insert(L, a, bi, lane);
+    list_insert(L, b, bi + 1, lane);
+    list_insert(L, c, bi + 2, lane);
+    list_insert(L, d, bi + 3, lane);
+  }
+}
+
+__device__ __forceinline__ void online_add(float& m, float& s, float x) {
+  if (x > m) {
+    s = s * __expf(m - x) + 1.f;
+    m = x;
+  } else if (m != -INFINITY) {
+    s += __expf(x - m);
+  }
+}
+
+__device__ __forceinline__ void online_add4(float& m, float& s, float4 x) {
+  float mx = fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w));
+  if (mx > m) {
+    s *= __expf(m - mx);  // m = -inf initially: exp(-inf) = 0
+    m = mx;
+  }
+  if (m != -INFINITY) s += __expf(x.x - m) + __expf(x.y - m) + __expf(x.z - m) + __expf(x.w - m);
+}
+
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p, int64_t i);  // elements i..i+3
+template <>
+__device__ __forceinline__ float4 load4<float>(const float* p, int64_t i) {
+  return __ldcs(reinterpret_cast<const float4*>(p + i));
+}
+template <>
+__device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p, int64_t i) {
+  uint2 u = __ldcs(reinterpret_cast<const uint2*>(p + i));
+  float4 r;
+  r.x = __uint_as_float(u.x << 16);
+  r.y = __uint_as_float(u.x & 0xffff0000u);
+  r.z = __uint_as_float(u.y << 16);
+  r.w = __uint_as_float(u.y & 0xffff0000u);
+  return r;
+}
+template <>
+__device__ __forceinline__ float4 load4<__half>(const __half* p, int64_t i) {
+  uint2 u = __ldcs(reinterpret_cast<const uint2*>(p + i));
+  __half2 a = *reinterpret_cast<__half2*>(&u.x), b = *reinterpret_cast<__half2*>(&u.y);
+  float2 fa = __half22float2(a), fb = __half22float2(b);
+  return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) score_kernel(const T* __restrict__ logits, int64_t ld_b, int64_t ld_s,
+                                                         int S, int V, float* __restrict__ lp,
+                                                         int32_t* __restrict__ ids, float* __restrict__ rest) {
+  const int row = blockIdx.x;  // b * S + s
+  const int b = row / S, s = row % S;
+  const T* x = logits + (int64_t)b * ld_b + (int64_t)s * ld_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  TopList L;
+  L.v = -INFINITY;
+  L.i = INT_MAX;
+  L.thr = -INFINITY;
+  L.thr_i = INT_MAX;
+  float m = -INFINITY, sum = 0.f;
+
+  // scalar head up to 16-byte alignment, vector body, scalar tail
+  int head = (int)((((uintptr_t)x + 15) & ~(uintptr_t)15) - (uintptr_t)x) / (int)sizeof(T);
+  if (head > V) head = V;
+  const int nvec = (V - head) / 4;
+  const int body_end = head + nvec * 4;
+  // vector body: every loop bound is block-uniform (warp-synchronous inserts)
+  const int stride = kThreads * 4;  // elements per block-wide vector sweep
+  int64_t base = head;
+  for (; base + 4 * stride <= body_end; base += 4 * stride) {
+    const int64_t e = base + (int64_t)tid * 4;
+    float4 vs[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) vs[r] = load4<T>(x, e + r * stride);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) online_add4(m, sum, vs[r]);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float mx = fmaxf(fmaxf(vs[r].x, vs[r].y), fmaxf(vs[r].z, vs[r].w));
+      offer4(L, mx >= L.thr, vs[r], (int)(e + r * stride), lane);
+    }
+  }
+  for (; base < body_end; base += stride) {
+    const int64_t e = base + (int64_t)tid * 4;
+    const bool in = e < body_end;  // body length is a multiple of 4
+    float4 v = in ? load4<T>(x, e) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (in) online_add4(m, sum, v);
+    float mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+    offer4(L, in && mx >= L.thr, v, (int)e, lane);
+  }
+  // scalar head and tail (fewer than 8 + 4 elements per row), warp 0
+  {
+    const int ntail = V - body_end;
+    const bool in = warp == 0 && lane < head + ntail;
+    const int idx = lane < head ? lane : body_end + (lane - head);
+    const float v = in ? to_f32(x[idx]) : -INFINITY;
+    if (in) online_add(m, sum, v);
+    unsigned msk = __ballot_sync(0xffffffffu, in && v >= L.thr);
+    while (msk) {
+      int src = __ffs(msk) - 1;
+      msk &= msk - 1;
+      list_insert(L, __shfl_sync(0xffffffffu, v, src), __shfl_sync(0xffffffffu, idx, src), lane);
+    }
+  }
+
+  // ---- block reduction of (max, sum) and of the 16 warp lists
+  __shared__ float s_m[kWarps], s_s[kWarps];
+  __shared__ float s_v[kWarps * kTopM];
+  __shared__ int s_i[kWarps * kTopM];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float om = __shfl_xor_sync(0xffffffffu, m, o);
+    float os = __shfl_xor_sync(0xffffffffu, sum, o);
+    float nm = fmaxf(m, om);
+    sum = (nm == -INFINITY) ? 0.f : sum * __expf(m - nm) + os * __expf(om - nm);
+    m = nm;
+  }
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_s[warp] = sum;
+  }
+  if (lane < kTopM) {
+    s_v[warp * kTopM + lane] = L.v;
+    s_i[warp * kTopM + lane] = L.i;
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  m = lane < kWarps ? s_m[lane] : -INFINITY;
+  sum = lane < kWarps ? s_s[lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float om = __shfl_xor_sync(0xffffffffu, m, o);
+    float os = __shfl_xor_sync(0xffffffffu, sum, o);
+    float nm = fmaxf(m, om);
+    sum = (nm == -INFINITY) ? 0.f : sum * __expf(m - nm) + os * __expf(om - nm);
+    m = nm;
+  }
+  // merge: warp 0 keeps its list and offers the other warps' entries
+  for (int c = kTopM; c < kWarps * kTopM; c += 32) {
+    const int j = c + lane;
+    const bool in = j < kWarps * kTopM;
+    float v = in ? s_v[j] : -INFINITY;
+    int i = in ? s_i[j] : INT_MAX;
+    unsigned msk = __ballot_sync(0xffffffffu, before(v, i, L.thr, L.thr_i));
+    while (msk) {
+      int src = __ffs(msk) - 1;
+      msk &= msk - 1;
+      list_insert(L, __shfl_sync(0xffffffffu, v, src), __shfl_sync(0xffffffffu, i, src), lane);
+    }
+  }
+  // log_softmax = (x - max) - log(sum exp(x - max)); rest from the 16 lp's
+  const float lse = logf(sum);
+  float lpv = lane < kTopM ? __fsub_rn(__fsub_rn(L.v, m), lse) : 0.f;
+  float ex = lane < kTopM ? expf(lpv) : 0.f;
+  float tot = warp_sum(ex);
+  if (lane < kTopM) {
+    lp[(int64_t)row * kTopM + lane] = lpv;
+    ids[(int64_t)row * kTopM + lane] = L.i;
+  }
+  if (lane == 0) rest[row] = logf(fminf(fmaxf(__fsub_rn(1.f, tot), 1e-6f), 1.0f));
+}
+
+}  // namespace
+
+int dft_score_launch(const dft_build_params* p, const void* logits, int32_t dtype, int64_t ld_b, int64_t ld_s,
+                     float* lp, int32_t* ids, float* rest, cudaStream_t st) {
+  dim3 grid((unsigned)(p->B * p->S));
+  switch (dtype) {
+    case DFT_F32:
+      score_kernel<float><<<grid, kThreads, 0, st>>>((const float*)logits, ld_b, ld_s, p->S, p->V, lp, ids, rest);
+      break;
+    case DFT_BF16:
+      score_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>((const __nv_bfloat16*)logits, ld_b, ld_s, p->S, p->V,
+                                                            lp, ids, rest);
+      break;
+    case DFT_F16:
+      score_kernel<__half><<<grid, kThreads, 0, st>>>((const __half*)logits, ld_b, ld_s, p->S, p->V, lp, ids, rest);
+      break;
+    default:
+      return DFT_ERR_INVALID;
+  }
+  DFT_LAUNCH_CHECK();
+  return DFT_OK;
+}
+
+extern "C" int dft_score(const dft_build_params* p, const void* logits, int32_t logits_dtype, int64_t ld_b,
+                         int64_t ld_s, float* lp, int32_t* ids, float* rest, void* stream) {
+  if (!p || !logits || !lp || !ids || !rest) return DFT_ERR_INVALID;
+  if (p->M != kTopM) return DFT_ERR_UNSUPPORTED;
+  if (p->B <= 0 || p->S <= 0 || p->V < kTopM || (int64_t)p->B * p->S > (1ll << 31) - 1) return DFT_ERR_INVALID;
+  return dft_score_launch(p, logits, logits_dtype, ld_b, ld_s, lp, ids, rest, reinterpret_cast<cudaStream_t>(stream));
+}

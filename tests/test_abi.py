@@ -1,0 +1,98 @@
+"""C-ABI checks that need no GPU: the library loads, exports every entry point
+declared in include/dforktree_b200.h, and the ctypes structs match the C
+layout (sizes and field offsets from a gcc-compiled probe of the header)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from dforktree_b200 import _lib as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "dforktree_b200.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"DFT_API\s+[\w\s\*]+?\b(dft_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(L.LIB_PATH):
+        from dforktree_b200 import build
+        build.build()
+    return L.load()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = _declared()
+    assert len(names) >= 16
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(L.SIGNATURES), "ctypes signatures must cover the header exactly"
+
+
+def test_status_strings_and_version(lib):
+    assert lib.dft_version() >= 10000
+    assert lib.dft_status_string(0) == b"ok"
+    assert b"invalid" in lib.dft_status_string(1)
+
+
+def test_invalid_arguments_are_rejected_on_the_host(lib):
+    # null pointers are rejected before any CUDA call (no device needed)
+    assert lib.dft_table_create(None, None, None) == 1
+    p = L.BuildParams(B=1, S=24, V=1000, M=15, N=32, lmax=99, use_ngram=1)
+    assert lib.dft_score_build_workspace_bytes(ctypes.byref(p)) == -1      # M must be 16
+    p.M = 16
+    p.N = 65
+    assert lib.dft_score_build_workspace_bytes(ctypes.byref(p)) == -1      # N <= 64
+    p.N = 32
+    assert lib.dft_score_build_workspace_bytes(ctypes.byref(p)) >= 23 * 4096 * 4
+    assert lib.dft_gdn_tree_verify(None, None, None) == 1
+    assert lib.dft_gdn_commit(None, None, None) == 1
+    assert lib.dft_tree_conv(None, None, None) == 1
+
+
+_PROBE = r"""
+#include <stddef.h>
+#include <stdio.h>
+#include "dforktree_b200.h"
+#define F(T, f) printf(#T " " #f " %zu\n", offsetof(T, f));
+int main(void) {
+  printf("dft_table_desc SIZE %zu\n", sizeof(dft_table_desc));
+  printf("dft_build_params SIZE %zu\n", sizeof(dft_build_params));
+  printf("dft_tree_out SIZE %zu\n", sizeof(dft_tree_out));
+  printf("dft_conv_args SIZE %zu\n", sizeof(dft_conv_args));
+  printf("dft_gdn_args SIZE %zu\n", sizeof(dft_gdn_args));
+  printf("dft_commit_args SIZE %zu\n", sizeof(dft_commit_args));
+  F(dft_table_desc, max_load) F(dft_table_desc, n4c) F(dft_build_params, lam_p)
+  F(dft_conv_args, iw_slots) F(dft_conv_args, y_dtype) F(dft_gdn_args, ag_sh) F(dft_gdn_args, pool)
+  F(dft_gdn_args, aux_k_per_v) F(dft_commit_args, ends) F(dft_commit_args, aux_k_per_v) F(dft_commit_args, so_sk)
+  return 0;
+}
+"""
+
+
+def test_ctypes_layout_matches_header(tmp_path):
+    src = tmp_path / "probe.c"
+    src.write_text(_PROBE)
+    exe = tmp_path / "probe"
+    r = subprocess.run(["gcc", "-std=c99", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)],
+                       capture_output=True, text=True)
+    if r.returncode != 0:
+        pytest.skip("gcc unavailable: " + r.stderr[:200])
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    structs = {"dft_table_desc": L.TableDesc, "dft_build_params": L.BuildParams, "dft_tree_out": L.TreeOut,
+               "dft_conv_args": L.ConvArgs, "dft_gdn_args": L.GdnArgs, "dft_commit_args": L.CommitArgs}
+    for line in out:
+        if not line:
+            continue
+        name, field, val = line.split()
+        cls = structs[name]
+        if field == "SIZE":
+            assert ctypes.sizeof(cls) == int(val), name
+        else:
+            assert getattr(cls, field).offset == int(val), (name, field)
