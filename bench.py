@@ -245,6 +245,12 @@ def run_ours(args, rank, world, local_rank):
     for _ in range(args.warmup):
         one_step()
     torch.cuda.synchronize()
+    if args.profile:
+        # profiling mode: just K plain cycles after the warm-up (for ncu)
+        for _ in range(args.steps):
+            one_step()
+        torch.cuda.synchronize()
+        return None
     # per-stage events on a separate pass of K steps (same work)
     mk = lambda: torch.cuda.Event(enable_timing=True)
     stage = {"score_build": 0.0, "conv_verify": 0.0, "accept": 0.0, "commit": 0.0}
@@ -434,6 +440,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="only W + K plain cycles (for ncu); prints nothing")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -443,7 +450,7 @@ def main():
             print(json.dumps(run_reference(args)), flush=True)
         return
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile:
         # before the first GPU call (spawned workers)
         workers = max(1, min(os.cpu_count() or 1, 64))
         sampler = CpuSampler(workers)
