@@ -105,6 +105,9 @@ SIGNATURES = {
     "dft_score_build_workspace_bytes": (i64, [C.POINTER(BuildParams)]),
     "dft_score_build": (C.c_int, [vp, C.POINTER(BuildParams), vp, i32, i64, i64, vp, vp, vp, C.POINTER(TreeOut),
                                   vp, vp]),
+    "dft_score_build_static_capacity": (i64, []),
+    "dft_score_build_static": (C.c_int, [vp, C.POINTER(BuildParams), vp, i32, i64, i64, vp, vp, C.POINTER(TreeOut),
+                                         vp, vp]),
     "dft_tree_struct": (C.c_int, [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
     "dft_accept_greedy": (C.c_int, [i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "dft_tree_conv": (C.c_int, [C.POINTER(ConvArgs), vp, vp]),

@@ -1,0 +1,96 @@
+// dft_score_build_static: score + build without a caller-supplied workspace.
+//
+// For callers that cannot allocate device memory: a plugin running inside a
+// serving engine's decode step, where HBM is owned by the engine's static
+// pools and torch's caching allocator (a raw cudaMalloc competes with pools
+// sized to fill the device, and cudaFree synchronises it), and C hosts that
+// bind only this ABI and have no device allocator of their own.  The scratch
+// that dft_score_build takes as `workspace` (drafter lp / ids / rest and the
+// dense PMI tensor T) lives here in one file-scope device array of fixed size,
+// held by every GPU that loads the library until the process exits.
+#include "dft_common.cuh"
+
+#include <mutex>
+
+int dft_score_launch(const dft_build_params* p, const void* logits, int32_t dtype, int64_t ld_b, int64_t ld_s,
+                     float* lp, int32_t* ids, float* rest, cudaStream_t st);
+int dft_beam_launch(const dft_build_params* p, const float* lp, const int32_t* ids, const float* rest, const float* T,
+                    const float* logc, const float* c0, const int64_t* root, const dft_tree_out* out,
+                    int32_t* dev_status, cudaStream_t st);
+int dft_pmi_dense_launch(const dft_table* table, const dft_build_params* p, const int32_t* ids, const int64_t* root,
+                         const int64_t* pre1, float* T, int32_t* dev_status, cudaStream_t st);
+int dft_check_build_params(const dft_build_params* p);
+
+namespace {
+
+// 32 MiB: 64 requests at S = 24 need 24.3 MB (lp, ids, rest and the dense
+// order-3 PMI tensor T of 23 x 16^3 floats per request).
+constexpr int64_t kStaticScratchBytes = 32ll << 20;
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_score_build_scratch[kStaticScratchBytes];
+
+std::mutex g_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+inline int64_t up256(int64_t x) { return (x + 255) & ~(int64_t)255; }
+
+// Device address of the scratch array for the current device, resolved once
+// per device with that device current (host code cannot use the symbol's
+// name as a device pointer).
+int scratch_for_current_device(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return DFT_ERR_NO_DEVICE;
+  if (dev >= kMaxDevices) return DFT_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_score_build_scratch) != cudaSuccess || !ptr) return DFT_ERR_CUDA;
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
+  return DFT_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t dft_score_build_static_capacity(void) { return kStaticScratchBytes; }
+
+extern "C" int dft_score_build_static(const dft_table* table, const dft_build_params* p, const void* logits,
+                                      int32_t logits_dtype, int64_t ld_b, int64_t ld_s, const int64_t* root,
+                                      const int64_t* pre1, dft_tree_out* out, int32_t* dev_status, void* stream) {
+  int rc = dft_check_build_params(p);
+  if (rc) return rc;
+  if (!logits || !root || !out) return DFT_ERR_INVALID;
+  if (p->use_ngram && !table) return DFT_ERR_INVALID;
+  if (!dft::valid_dtype(logits_dtype)) return DFT_ERR_INVALID;
+  if (ld_s < p->V || ld_b < (int64_t)p->S * ld_s - (ld_s - p->V)) return DFT_ERR_INVALID;
+  // scratch layout identical to dft_score_build's workspace
+  const int64_t rows = (int64_t)p->B * p->S;
+  const int64_t o_lp = 0;
+  const int64_t o_ids = up256(o_lp + rows * p->M * 4);
+  const int64_t o_rest = up256(o_ids + rows * p->M * 4);
+  const int64_t o_T = up256(o_rest + rows * 4);
+  const int64_t total =
+      up256(o_T + (p->use_ngram ? (int64_t)p->B * (p->S - 1) * p->M * p->M * p->M * 4 : 0));
+  if (total > kStaticScratchBytes) return DFT_ERR_CAPACITY;
+  void* base = nullptr;
+  rc = scratch_for_current_device(&base);
+  if (rc) return rc;
+  char* ws = reinterpret_cast<char*>(base);
+  float* lp = reinterpret_cast<float*>(ws + o_lp);
+  int32_t* ids = reinterpret_cast<int32_t*>(ws + o_ids);
+  float* rest = reinterpret_cast<float*>(ws + o_rest);
+  float* T = p->use_ngram ? reinterpret_cast<float*>(ws + o_T) : nullptr;
+  // every scratch byte read below is written earlier in the same call (score
+  // writes all lp / ids / rest rows, the PMI kernel all of T): nothing needs
+  // clearing between calls
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = dft_score_launch(p, logits, logits_dtype, ld_b, ld_s, lp, ids, rest, st);
+  if (rc) return rc;
+  if (p->use_ngram && p->S > 1) {
+    rc = dft_pmi_dense_launch(table, p, ids, root, pre1, T, dev_status, st);
+    if (rc) return rc;
+  }
+  return dft_beam_launch(p, lp, ids, rest, T, nullptr, nullptr, root, out, dev_status, st);
+}

@@ -177,6 +177,20 @@ def score_build(table, logits, root, pre1, N, workspace, out, lmax=99, chain_fir
     return out
 
 
+def score_build_static(table, logits, root, pre1, N, out, lmax=99, chain_first=False, use_ngram=True, lam_a=0.3,
+                       lam_p=0.6, status=None):
+    """score_build without a workspace: the library's fixed-size device
+    scratch (dft_score_build_static); for callers that cannot allocate."""
+    lib = L.lib()
+    x, B, S, V, sb, ss = _logits_view(logits)
+    p = build_params(B, S, V, N, 16, lmax, chain_first, use_ngram, lam_a, lam_p)
+    to = _tree_struct_out(out)
+    L.check(lib.dft_score_build_static(None if table is None else table.handle, C.byref(p), x.data_ptr(),
+                                       L.dtype_code(x), sb, ss, root.data_ptr(), L.ptr(pre1), C.byref(to),
+                                       _status_ptr(status), L.stream_handle()), "dft_score_build_static")
+    return out
+
+
 def tree_struct(parent: torch.Tensor, status=None):
     """anc [B,N,N], depth, cidx [B,N,4], nxt, sib for parent [B,N] (root first)."""
     lib = L.lib()

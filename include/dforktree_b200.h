@@ -36,7 +36,8 @@ enum {
   DFT_ERR_UNSUPPORTED = 2,  /* shape outside what the kernels implement    */
   DFT_ERR_CUDA = 3,         /* CUDA runtime error (launch, allocation)     */
   DFT_ERR_TABLE = 4,        /* n-gram keys unsorted, negative or too many  */
-  DFT_ERR_NO_DEVICE = 5     /* no sm_100 device current                    */
+  DFT_ERR_NO_DEVICE = 5,    /* no sm_100 device current                    */
+  DFT_ERR_CAPACITY = 6      /* larger than a fixed-size static scratch     */
 };
 enum {
   DFT_DEV_BAD_TOKEN = 1,    /* token id outside [-V, V)                    */
@@ -138,6 +139,26 @@ DFT_API int64_t dft_score_build_workspace_bytes(const dft_build_params* p);
 DFT_API int dft_score_build(const dft_table* table, const dft_build_params* p, const void* logits, int32_t logits_dtype,
                     int64_t ld_b, int64_t ld_s, const int64_t* root, const int64_t* pre1, void* workspace,
                     dft_tree_out* out, int32_t* dev_status, void* stream);
+
+/* Allocation-free score + build.  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory -- a plugin inside a serving
+ * engine's decode step, whose HBM belongs to the engine's static pools and to
+ * torch's caching allocator (a raw cudaMalloc competes with pools sized to
+ * fill the device; cudaFree synchronises it), or a C host that binds only
+ * this ABI and has no device allocator.  Same inputs, outputs and kernels as
+ * dft_score_build, but the scratch lives in one file-scope device array of
+ * dft_score_build_static_capacity() bytes (32 MiB: 64 requests at S = 24),
+ * held by every GPU that loads the library until the process exits; larger
+ * shapes return DFT_ERR_CAPACITY.  The first call on a device resolves the
+ * array's device address (cudaGetSymbolAddress, with that device current);
+ * make that first call before any stream capture.  All calls share the one
+ * array: calls whose kernels overlap on the GPU (other streams, other host
+ * threads) race.  Each call writes every scratch byte it reads, so nothing
+ * carries over between calls.  Allocates nothing. */
+DFT_API int64_t dft_score_build_static_capacity(void);
+DFT_API int dft_score_build_static(const dft_table* table, const dft_build_params* p, const void* logits,
+                                   int32_t logits_dtype, int64_t ld_b, int64_t ld_s, const int64_t* root,
+                                   const int64_t* pre1, dft_tree_out* out, int32_t* dev_status, void* stream);
 
 /* Tree structure for a caller-given topology (tree_ops.tree_struct,
  * tree_ops.py:68-89, plus nxt/sib of fc1_builder.py:41-47).  parent [B, N]
