@@ -36,6 +36,8 @@ S, V, N, M, LAYERS, HK, HV, D = 24, 248320, 32, 16, 24, 16, 32, 128
 C_CONV = 2 * HK * D + HV * D
 # algorithmic bytes per unit (per layer-request), see DESIGN.md
 VERIFY_BYTES = 2 * 1024 * 1024 + 262144 + 262144 + 8192 + 262144      # S0 + q,k + v + g,beta + o
+# the fused launch also reads the conv state / weights and writes the aux rows the commit needs
+VERIFY_AUX_BYTES = 8192 * 3 * 2 + 262144 + 524288 + 4096               # conv state + k_hat + vn + G
 COMMIT_BYTES_FIXED = 4 * 1024 * 1024                                   # read S0 + write S
 COMMIT_BYTES_PER_NODE = 32 * 1024                                      # k, vn rows of 32 heads
 SCORE_BYTES = S * V * 4 + 105984 * 12 + 2944                           # logits + table probes + prev/pn
@@ -265,27 +267,21 @@ def run_ours(args, rank, world, local_rank):
         stage["conv_verify"] += ev["sb1"].elapsed_time(ev["v1"])
         stage["accept"] += ev["v1"].elapsed_time(ev["c0"])
         stage["commit"] += ev["c0"].elapsed_time(ev["c1"])
-    # per-launch verify duration: conv and verify timed separately on one pass
-    conv_ms = verify_ms = 0.0
+    # per-launch duration of the fused conv + GDN verify (the dominant kernel)
+    verify_ms = 0.0
     pairs = []
     for _ in range(args.steps):
         cyc.build(logits, root, pre1)
         for l in range(cfg.layers):
-            e0, e1, e2 = mk(), mk(), mk()
-            c = cyc.cfg
-            e0.record(stream)
-            K.tree_conv(x[l], cyc.conv_state[l], cyc.conv_w[l], None, cyc.tree["cidx"], y=cyc.y)
+            e1, e2 = mk(), mk()
             e1.record(stream)
-            K.gdn_tree_verify(cyc.y, a[l], b[l], None, cyc.dt_bias[l], cyc.tree["anc"], cyc.pool[l], c.Hk, c.Hv,
-                              c.D, c.D, neg_exp_A=cyc.neg_exp_A[l], o=cyc.o, aux_k=cyc.aux_k[l],
-                              aux_vn=cyc.aux_vn[l], aux_g=cyc.aux_g[l], aux_k_per_v=False)
+            cyc.verify_layer(l, x[l], a[l], b[l])
             e2.record(stream)
-            pairs.append((e0, e1, e2))
+            pairs.append((e1, e2))
         cyc.accept(target_fn(cyc.tree))
         cyc.commit()
     torch.cuda.synchronize()
-    for e0, e1, e2 in pairs:
-        conv_ms += e0.elapsed_time(e1)
+    for e1, e2 in pairs:
         verify_ms += e1.elapsed_time(e2)
     n_verify = len(pairs)
 
@@ -375,8 +371,7 @@ def run_ours(args, rank, world, local_rank):
             "traffic": traffic.get(dom)}
     per_kernel = {
         "score_build_ms": stage["score_build"] / args.steps,
-        "tree_conv_ms_per_layer": conv_ms / max(n_verify, 1),
-        "gdn_verify_ms_per_layer": verify_launch_ms,
+        "conv_verify_ms_per_layer": verify_launch_ms,
         "accept_ms": stage["accept"] / args.steps,
         "gdn_commit_ms": commit_launch_ms,
         "score_build_GBps": Bt * SCORE_BYTES / (stage["score_build"] / args.steps / 1e3) / 1e9,

@@ -61,6 +61,12 @@ class ConvArgs(C.Structure):
                 ("iw_slots", vp)]
 
 
+class GdnConvArgs(C.Structure):
+    _fields_ = [("x", vp), ("x_dtype", i32), ("x_sb", i64), ("x_sn", i64),
+                ("conv_state", vp), ("cs_dtype", i32), ("cs_ss", i64), ("cs_sc", i64), ("cs_st", i64),
+                ("conv_slots", vp), ("weight", vp), ("w_dtype", i32), ("bias", vp), ("cidx", vp)]
+
+
 class GdnArgs(C.Structure):
     _fields_ = [("B", i32), ("N", i32), ("Hk", i32), ("Hv", i32), ("Dk", i32), ("Dv", i32),
                 ("scale", f32),
@@ -69,12 +75,13 @@ class GdnArgs(C.Structure):
                 ("A_log", vp), ("neg_exp_A", vp),
                 ("dt_bias", vp), ("dtb_dtype", i32),
                 ("anc", vp),
-                ("pool", vp), ("p_ss", i64), ("p_sh", i64), ("p_sv", i64), ("p_sk", i64),
+                ("pool", vp), ("p_ss", i64), ("p_sh", i64), ("p_sv", i64), ("p_sk", i64), ("p_nslots", i64),
                 ("state_slots", vp),
                 ("o", vp), ("o_dtype", i32), ("o_sb", i64), ("o_sn", i64), ("o_sh", i64),
                 ("aux_k", vp), ("aux_k_per_v", i32), ("ak_sb", i64), ("ak_sh", i64), ("ak_sn", i64),
                 ("aux_vn", vp), ("av_sb", i64), ("av_sh", i64), ("av_sn", i64),
-                ("aux_g", vp), ("ag_sb", i64), ("ag_sh", i64)]
+                ("aux_g", vp), ("ag_sb", i64), ("ag_sh", i64),
+                ("conv", C.POINTER(GdnConvArgs)), ("force_simt", i32)]
 
 
 class CommitArgs(C.Structure):

@@ -228,12 +228,15 @@ int launch_simt(const dft_gdn_args& a, int32_t* st, cudaStream_t s) {
 }  // namespace
 
 int dft_gdn_check(const dft_gdn_args* a) {
-  if (!a || !a->y || !a->a || !a->bg || !a->dt_bias || !a->anc || !a->pool || !a->o) return DFT_ERR_INVALID;
+  if (!a || (!a->y && !a->conv) || !a->a || !a->bg || !a->dt_bias || !a->anc || !a->pool || !a->o) return DFT_ERR_INVALID;
   if (!a->A_log && !a->neg_exp_A) return DFT_ERR_INVALID;
   if (a->B <= 0 || a->B > 65535 || a->N < 1 || a->Hk <= 0 || a->Hv <= 0) return DFT_ERR_INVALID;
   if (a->Hv % a->Hk) return DFT_ERR_INVALID;
   if (a->Dk != kD || a->Dv != kD || a->N > kMaxNodes) return DFT_ERR_UNSUPPORTED;
-  if (!valid_dtype(a->y_dtype) || !valid_dtype(a->ab_dtype) || !valid_dtype(a->dtb_dtype) ||
+  if (a->conv && (!a->conv->x || !a->conv->conv_state || !a->conv->weight || !a->conv->cidx ||
+                  !valid_dtype(a->conv->x_dtype) || !valid_dtype(a->conv->cs_dtype) || !valid_dtype(a->conv->w_dtype)))
+    return DFT_ERR_INVALID;
+  if ((!a->conv && !valid_dtype(a->y_dtype)) || !valid_dtype(a->ab_dtype) || !valid_dtype(a->dtb_dtype) ||
       !valid_dtype(a->o_dtype))
     return DFT_ERR_INVALID;
   if (a->aux_k && (a->ak_sn % 4 || a->ak_sb % 4 || a->ak_sh % 4 || ((uintptr_t)a->aux_k & 15)))
@@ -241,12 +244,20 @@ int dft_gdn_check(const dft_gdn_args* a) {
   return DFT_OK;
 }
 
+bool dft_gdn_tc_applicable(const dft_gdn_args* a);
+int dft_gdn_tc_launch(const dft_gdn_args* a, int32_t* status, cudaStream_t st);
+
 extern "C" int dft_gdn_tree_verify(const dft_gdn_args* args, int32_t* dev_status, void* stream) {
   int rc = dft_gdn_check(args);
   if (rc) return rc;
   dft_gdn_args a = *args;
-  if (a.scale == 0.f) a.scale = 1.f / sqrtf((float)a.Dk);
+  if (a.scale == 0.f) a.scale = (float)(1.0 / sqrt((double)a.Dk));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dft_gdn_tc_applicable(&a)) {
+    rc = dft_gdn_tc_launch(&a, dev_status, s);
+    if (rc != DFT_ERR_UNSUPPORTED || a.conv) return rc;   // tensor map refused: fall back to SIMT
+  }
+  if (a.conv) return DFT_ERR_UNSUPPORTED;   // the fused tree conv lives in the tcgen05 path
   if (a.N <= 32) return launch_simt<32>(a, dev_status, s);
   return launch_simt<64>(a, dev_status, s);
 }

@@ -79,7 +79,7 @@ class DraftTreeCycle:
         p = self.pool
         self.pool_out = torch.as_strided(p, (Ls, B, 1, c.Hv, D, D),
                                          (p.stride(0), p.stride(1), 0, p.stride(2), p.stride(3), p.stride(4)))
-        self.launches_per_step = 3 + 2 * Ls + 1 + 1
+        self.launches_per_step = 3 + Ls + 1 + 1
 
     # -- stages --------------------------------------------------------------
     def build(self, logits, root, pre1):
@@ -88,6 +88,15 @@ class DraftTreeCycle:
                       status=self.status)
 
     def verify_layer(self, l, x, a, b):
+        """Tree conv fused into the GDN tree verify of layer l (one launch)."""
+        c = self.cfg
+        conv = dict(x=x, conv_state=self.conv_state[l], weight=self.conv_w[l], cidx=self.tree["cidx"])
+        K.gdn_tree_verify(None, a, b, None, self.dt_bias[l], self.tree["anc"], self.pool[l], c.Hk, c.Hv, c.D, c.D,
+                          neg_exp_A=self.neg_exp_A[l], o=self.o, aux_k=self.aux_k[l], aux_vn=self.aux_vn[l],
+                          aux_g=self.aux_g[l], aux_k_per_v=False, status=self.status, conv=conv)
+
+    def verify_layer_unfused(self, l, x, a, b):
+        """Separate tree conv launch, then the verify (the plugin's hook order)."""
         c = self.cfg
         K.tree_conv(x, self.conv_state[l], self.conv_w[l], None, self.tree["cidx"], y=self.y, status=self.status)
         K.gdn_tree_verify(self.y, a, b, None, self.dt_bias[l], self.tree["anc"], self.pool[l], c.Hk, c.Hv, c.D, c.D,

@@ -257,20 +257,24 @@ def tree_conv(x, conv_state, weight, bias, cidx, state_slots=None, y=None, iw=No
 # -------------------------------------------------------- GDN tree verify --
 def gdn_tree_verify(y, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk=128, Dv=128, state_slots=None, scale=None,
                     neg_exp_A=None, o=None, aux_k=None, aux_vn=None, aux_g=None, aux_k_per_v=True, status=None,
-                    pool_strides=None):
+                    pool_strides=None, pool_nslots=None, conv=None, force_simt=False):
     """Batched tree GDN verify.
 
-    y [B, N, 2*Hk*Dk + Hv*Dv] (last stride 1); a, b [B, N, Hv] (last stride 1);
+    y [B, N, 2*Hk*Dk + Hv*Dv] (last stride 1) -- or None with conv = dict(x=[B, N, C]
+    pre-conv inputs, conv_state=[slots, C, 3], weight=[C, 4], bias=None|[C],
+    cidx=[B, N, 4], conv_slots=None|[B]) to fuse the tree conv;
+    a, b [B, N, Hv] (last stride 1);
     pool [slots, Hv, Dv, Dk] (any strides; `pool_strides` = (slot, h, v, k)
     element strides overrides pool.stride() for views torch cannot express);
     anc [B, N, N] f32; o [B, N, Hv, Dv].
     aux_k [B, Hv or Hk, N, Dk], aux_vn [B, Hv, N, Dv], aux_g [B, Hv, N].
     """
     lib = L.lib()
-    B, N, _ = y.shape
-    assert y.stride(2) == 1 and a.stride(2) == 1 and b.stride(2) == 1 and a.stride() == b.stride()
+    ref = y if y is not None else conv["x"]
+    B, N, _ = ref.shape
+    assert ref.stride(2) == 1 and a.stride(2) == 1 and b.stride(2) == 1 and a.stride() == b.stride()
     if o is None:
-        o = torch.empty(B, N, Hv, Dv, dtype=y.dtype, device=y.device)
+        o = torch.empty(B, N, Hv, Dv, dtype=ref.dtype, device=ref.device)
     assert o.stride(3) == 1
     anc = anc.reshape(B, N, N).to(torch.float32).contiguous()
     if scale is None:
@@ -279,12 +283,30 @@ def gdn_tree_verify(y, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk=128, Dv=128, 
     neg = None if neg_exp_A is None else neg_exp_A.to(torch.float32).contiguous()
     dtb = dt_bias.contiguous()
     ps = tuple(pool.stride()) if pool_strides is None else tuple(int(x) for x in pool_strides)
+    nslots = int(pool.shape[0]) if pool_nslots is None and pool_strides is None else int(pool_nslots or 0)
+    cv = None
+    keep_cv = ()
+    if conv is not None:
+        x = conv["x"]
+        cs = conv["conv_state"]
+        w = conv["weight"].reshape(-1, 4).contiguous()
+        bias = conv.get("bias")
+        bias = None if bias is None else bias.to(w.dtype).contiguous()
+        cidx = conv["cidx"].reshape(B, N, 4).to(torch.int64).contiguous()
+        cslots = conv.get("conv_slots")
+        cslots = None if cslots is None else cslots.to(torch.int64).contiguous()
+        cv = L.GdnConvArgs(x=x.data_ptr(), x_dtype=L.dtype_code(x), x_sb=x.stride(0), x_sn=x.stride(1),
+                           conv_state=cs.data_ptr(), cs_dtype=L.dtype_code(cs), cs_ss=cs.stride(0),
+                           cs_sc=cs.stride(1), cs_st=cs.stride(2), conv_slots=L.ptr(cslots), weight=w.data_ptr(),
+                           w_dtype=L.dtype_code(w), bias=L.ptr(bias), cidx=cidx.data_ptr())
+        keep_cv = (w, bias, cidx, cslots)
     args = L.GdnArgs(B=B, N=N, Hk=Hk, Hv=Hv, Dk=Dk, Dv=Dv, scale=float(scale),
-                     y=y.data_ptr(), y_dtype=L.dtype_code(y), y_sb=y.stride(0), y_sn=y.stride(1),
+                     y=L.ptr(y), y_dtype=L.dtype_code(y) if y is not None else 0,
+                     y_sb=y.stride(0) if y is not None else 0, y_sn=y.stride(1) if y is not None else 0,
                      a=a.data_ptr(), bg=b.data_ptr(), ab_dtype=L.dtype_code(a), ab_sb=a.stride(0), ab_sn=a.stride(1),
                      A_log=L.ptr(A_log_f), neg_exp_A=L.ptr(neg), dt_bias=dtb.data_ptr(), dtb_dtype=L.dtype_code(dtb),
                      anc=anc.data_ptr(), pool=pool.data_ptr(), p_ss=ps[0], p_sh=ps[1], p_sv=ps[2], p_sk=ps[3],
-                     state_slots=L.ptr(state_slots),
+                     p_nslots=nslots, state_slots=L.ptr(state_slots),
                      o=o.data_ptr(), o_dtype=L.dtype_code(o), o_sb=o.stride(0), o_sn=o.stride(1), o_sh=o.stride(2),
                      aux_k=L.ptr(aux_k), aux_k_per_v=int(bool(aux_k_per_v)),
                      ak_sb=aux_k.stride(0) if aux_k is not None else 0,
@@ -294,8 +316,9 @@ def gdn_tree_verify(y, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk=128, Dv=128, 
                      av_sh=aux_vn.stride(1) if aux_vn is not None else 0,
                      av_sn=aux_vn.stride(2) if aux_vn is not None else 0,
                      aux_g=L.ptr(aux_g), ag_sb=aux_g.stride(0) if aux_g is not None else 0,
-                     ag_sh=aux_g.stride(1) if aux_g is not None else 0)
-    keep = (anc, A_log_f, neg, dtb)
+                     ag_sh=aux_g.stride(1) if aux_g is not None else 0,
+                     conv=C.pointer(cv) if cv is not None else None, force_simt=int(bool(force_simt)))
+    keep = (anc, A_log_f, neg, dtb, keep_cv, cv)
     L.check(lib.dft_gdn_tree_verify(C.byref(args), _status_ptr(status), L.stream_handle()), "dft_gdn_tree_verify")
     del keep
     return o

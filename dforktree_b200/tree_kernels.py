@@ -39,6 +39,9 @@ def tree_gdn_split(y, aa0, bb0, A_log, dt_bias, S0, Anc, Hk, Hv, Dk, Dv, scale=N
     # pool element (slot, h, v, k) = S0[h, k, v] + slot * state_slot_stride
     s_h, s_k, s_v = S0.stride()
     strides = (int(state_slot_stride) if state_indices is not None else 0, s_h, s_v, s_k)
+    # slots addressable from S0's base (bounds the state TMA)
+    avail = S0.untyped_storage().nbytes() // S0.element_size() - S0.storage_offset()
+    nslots = max(1, avail // int(state_slot_stride)) if state_indices is not None and state_slot_stride else 1
     slots = None
     if state_indices is not None:
         slots = state_indices.reshape(-1)[:1].to(torch.int64)
@@ -48,7 +51,7 @@ def tree_gdn_split(y, aa0, bb0, A_log, dt_bias, S0, Anc, Hk, Hv, Dk, Dv, scale=N
         ak, av, ag = aux[0].unsqueeze(0), aux[1].unsqueeze(0), aux[2].unsqueeze(0)
     K.gdn_tree_verify(y.unsqueeze(0), aa0.unsqueeze(0), bb0.unsqueeze(0), A_log, dt_bias, Anc.unsqueeze(0), S0, Hk,
                       Hv, Dk, Dv, state_slots=slots, scale=scale, neg_exp_A=neg_exp_A, o=o, aux_k=ak, aux_vn=av,
-                      aux_g=ag, aux_k_per_v=True, pool_strides=strides)
+                      aux_g=ag, aux_k_per_v=True, pool_strides=strides, pool_nslots=nslots)
     return o[0]
 
 

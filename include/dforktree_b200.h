@@ -203,7 +203,19 @@ DFT_API int dft_tree_conv(const dft_conv_args* a, int32_t* dev_status, void* str
  * columns [q (Hk*Dk) | k (Hk*Dk) | v (Hv*Dv)]; a, bg (b, n, h); state pool
  * element (slot, h, v, k) -- V-major like SGLang's ssm pool; o (b, n, h, v).
  * aux (all optional): k_hat (b, head, n, k) for head = v-head (aux_k_per_v=1,
- * the reference's CTX.keys layout) or k-head; vn (b, h, n, v); G (b, h, n). */
+ * the reference's CTX.keys layout) or k-head; vn (b, h, n, v); G (b, h, n).
+ * With `conv` set, y is not read: the tree conv of fc1_conv.py:8-27 is
+ * computed from the pre-conv inputs inside the verifier (the window taps
+ * are not written; dft_tree_conv does that for the drop-in hook). */
+typedef struct {
+  const void* x; int32_t x_dtype; int64_t x_sb, x_sn;   /* pre-conv (b, n, col), col stride 1 */
+  const void* conv_state; int32_t cs_dtype; int64_t cs_ss, cs_sc, cs_st;
+  const int64_t* conv_slots;      /* [B]; NULL: slot b                      */
+  const void* weight; int32_t w_dtype;                  /* [C, 4]         */
+  const void* bias;               /* [C] or NULL, dtype w_dtype             */
+  const int64_t* cidx;            /* [B, N, 4] conv columns                 */
+} dft_gdn_conv_args;
+
 typedef struct {
   int32_t B, N, Hk, Hv, Dk, Dv;
   float scale;                    /* 0 -> Dk^-0.5                           */
@@ -214,11 +226,14 @@ typedef struct {
   const void* dt_bias; int32_t dtb_dtype;
   const float* anc;               /* [B, N, N]                              */
   const float* pool; int64_t p_ss, p_sh, p_sv, p_sk;
+  int64_t p_nslots;               /* slots addressable in the pool (bounds the state TMA); 0: unknown */
   const int64_t* state_slots;     /* [B]; NULL: slot b; negative -> 0       */
   void* o; int32_t o_dtype; int64_t o_sb, o_sn, o_sh;
   float* aux_k; int32_t aux_k_per_v; int64_t ak_sb, ak_sh, ak_sn;
   float* aux_vn; int64_t av_sb, av_sh, av_sn;
   float* aux_g; int64_t ag_sb, ag_sh;
+  const dft_gdn_conv_args* conv;  /* NULL: read y                           */
+  int32_t force_simt;             /* 1: CUDA-core path even where the tcgen05 path applies */
 } dft_gdn_args;
 DFT_API int dft_gdn_tree_verify(const dft_gdn_args* a, int32_t* dev_status, void* stream);
 

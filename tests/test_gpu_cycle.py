@@ -1,0 +1,155 @@
+"""GPU: the tcgen05 GDN verifier (fused tree conv) and the batched cycle.
+
+* fused conv + verify == separate conv launch + verify (same arithmetic);
+* tcgen05 path vs the CUDA-core path vs the CPU oracle at the Qwen3.5 head
+  shape, fp32 and bf16 activations;
+* one DraftTreeCycle step (score -> build -> conv+verify per layer -> greedy
+  accept -> in-place commit) against the oracle chain, request by request.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import builder as OB
+from oracle import gdn as OG
+from oracle import ngram as ON
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from dforktree_b200 import build
+    build.build()
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _rel(a, b):
+    return float(np.abs(np.asarray(a, np.float64) - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def _layer_inputs(B, N, Hk, Hv, D, seed, dtype, chain_p=0.5):
+    from dforktree_b200 import kernels as K
+    from dforktree_b200 import synth
+    rng = np.random.default_rng(seed)
+    C = 2 * Hk * D + Hv * D
+    par = np.stack([synth.random_tree_parents(N, rng, chain_p=chain_p * (b % 2)) for b in range(B)])
+    parent = torch.from_numpy(par).to(DEV)
+    anc, depth, cidx, nxt, sib = K.tree_struct(parent)
+    g = torch.Generator(device=DEV)
+    g.manual_seed(seed)
+    x = torch.randn(B, N, C, device=DEV, generator=g).to(dtype)
+    conv_state = torch.randn(B, C, 3, device=DEV, generator=g).to(dtype)
+    weight = (torch.randn(C, 4, device=DEV, generator=g) * 0.5).to(dtype)
+    a = torch.randn(B, N, Hv, device=DEV, generator=g).to(dtype)
+    b = torch.randn(B, N, Hv, device=DEV, generator=g).to(dtype)
+    pool = torch.randn(B, Hv, D, D, device=DEV, generator=g) * 0.02
+    A_log = torch.randn(Hv, device=DEV, generator=g) * 0.5
+    dtb = torch.randn(Hv, device=DEV, generator=g) * 0.5
+    return dict(par=par, anc=anc, cidx=cidx, x=x, conv_state=conv_state, weight=weight, a=a, b=b, pool=pool,
+                A_log=A_log, dtb=dtb)
+
+
+def _verify(d, Hk, Hv, y=None, conv=False, force_simt=False):
+    from dforktree_b200 import kernels as K
+    B, N = d["a"].shape[:2]
+    ak = torch.zeros(B, Hk, N, 128, device=DEV)
+    av = torch.zeros(B, Hv, N, 128, device=DEV)
+    ag = torch.zeros(B, Hv, N, device=DEV)
+    cv = dict(x=d["x"], conv_state=d["conv_state"], weight=d["weight"], cidx=d["cidx"]) if conv else None
+    o = K.gdn_tree_verify(y, d["a"], d["b"], d["A_log"], d["dtb"], d["anc"], d["pool"], Hk, Hv, aux_k=ak,
+                          aux_vn=av, aux_g=ag, aux_k_per_v=False, conv=cv, force_simt=force_simt,
+                          o=torch.empty(B, N, Hv, 128, dtype=d["x"].dtype, device=DEV))
+    return o, ak, av, ag
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_conv_verify_equals_separate_conv_then_verify(dtype):
+    from dforktree_b200 import kernels as K
+    Hk, Hv = 16, 32
+    d = _layer_inputs(4, 32, Hk, Hv, 128, seed=31, dtype=dtype)
+    y = K.tree_conv(d["x"], d["conv_state"], d["weight"], None, d["cidx"])
+    ref = _verify(d, Hk, Hv, y=y)
+    got = _verify(d, Hk, Hv, conv=True)
+    for r, g_ in zip(ref, got):
+        assert torch.equal(r, g_)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-3), (torch.bfloat16, 2e-2)])
+@pytest.mark.parametrize("N", [32, 20, 1])
+def test_tensor_core_verify_matches_simt_and_oracle(dtype, tol, N):
+    from dforktree_b200 import kernels as K
+    Hk, Hv, D = 16, 32, 128
+    d = _layer_inputs(3, N, Hk, Hv, D, seed=40 + N, dtype=dtype)
+    y = K.tree_conv(d["x"], d["conv_state"], d["weight"], None, d["cidx"])
+    tc = _verify(d, Hk, Hv, y=y)
+    si = _verify(d, Hk, Hv, y=y, force_simt=True)
+    assert _rel(_np(tc[0]), _np(si[0])) < tol
+    assert _rel(_np(tc[2]), _np(si[2])) < 1e-3
+    assert _rel(_np(tc[1]), _np(si[1])) < 1e-5
+    for r in range(3):
+        anc = _np(d["anc"][r])
+        oo, ok, ovn, oG = OG.tree_gdn(_np(y[r]), _np(d["a"][r]), _np(d["b"][r]), _np(d["A_log"]), _np(d["dtb"]),
+                                      _np(d["pool"]), r, anc, Hk, Hv, D, D)
+        assert _rel(_np(tc[0][r]), oo) < tol, r
+        assert _rel(_np(tc[2][r]), ovn) < 1e-3, r
+        np.testing.assert_allclose(_np(tc[3][r]), oG, rtol=1e-5, atol=1e-5)
+
+
+def test_cycle_step_matches_oracle_chain():
+    """One batched cycle (B=4, 2 GDN layers, V=2048) request by request."""
+    from dforktree_b200 import kernels as K
+    from dforktree_b200 import synth
+    from dforktree_b200.cycle import CycleConfig, DraftTreeCycle
+    from dforktree_b200.ngram_gpu import load_npz_arrays
+    V, S, N, B, Ls = 2048, 24, 32, 4, 2
+    table = synth.make_ngram_table(V, 60000, 200000, seed=77)
+    cfg = CycleConfig(B=B, S=S, V=V, N=N, layers=Ls)
+    cyc = DraftTreeCycle(cfg, K.Table(load_npz_arrays(table), beta3=60.0), DEV, seed=5)
+    pool0 = cyc.pool.clone()
+    logits = np.stack([synth.make_logits(S, V, seed=600 + r) for r in range(B)])
+    lt = torch.from_numpy(logits).to(DEV)
+    root = torch.tensor([11, 22, 33, 44], device=DEV)
+    pre1 = torch.tensor([1, 2, 3, 4], device=DEV)
+    g = torch.Generator(device=DEV)
+    g.manual_seed(9)
+    x = torch.randn(Ls, B, N, cfg.C, device=DEV, generator=g).to(torch.bfloat16)
+    a = torch.randn(Ls, B, N, cfg.Hv, device=DEV, generator=g).to(torch.bfloat16)
+    b = torch.randn(Ls, B, N, cfg.Hv, device=DEV, generator=g).to(torch.bfloat16)
+    acc_len = torch.tensor([1, 3, 6, 24], device=DEV)
+
+    def target_fn(tree):
+        nx = tree["nxt"]
+        tgt = torch.gather(tree["tokens"], 1, nx.clamp(min=0))
+        keep = (nx >= 0) & (tree["depth"] + 1 < acc_len[:, None])
+        return torch.where(keep, tgt, torch.full_like(tgt, -1))
+
+    cyc.step(lt, root, pre1, x, a, b, target_fn)
+    torch.cuda.synchronize()
+    assert int(cyc.status.item()) == 0
+    ong = ON.NGramOracle(table, beta3=60.0)
+    path = cyc.path.cpu().numpy()
+    for r in range(B):
+        tr = OB.builder_run(logits[r], int(root[r]), int(pre1[r]), ong, N=N)
+        assert np.array_equal(cyc.tree["tokens"][r].cpu().numpy(), tr["tokens"])
+        assert np.array_equal(cyc.tree["parent"][r].cpu().numpy(), tr["parent"])
+        # accepted path: first-child chain, length min(acc_len, chain depth)
+        p = [0]
+        while len(p) < int(acc_len[r]) and tr["nxt"][p[-1]] >= 0:
+            p.append(int(tr["nxt"][p[-1]]))
+        assert list(path[r][: len(p)]) == p and np.all(path[r][len(p):] == -1)
+        for l in range(Ls):
+            xr = _np(x[l, r])
+            y, _ = OG.tree_conv(xr, _np(cyc.conv_state[l, r]), _np(cyc.conv_w[l]), None, tr["cidx"])
+            y = _np(torch.from_numpy(y).to(torch.bfloat16))      # the conv output is stored in x's dtype
+            o, k, vn, G = OG.tree_gdn(y, _np(a[l, r]), _np(b[l, r]), _np(cyc.A_log[l]), _np(cyc.dt_bias[l]),
+                                      _np(pool0[l]), r, tr["anc"], cfg.Hk, cfg.Hv, 128, 128)
+            for h in range(cfg.Hv):
+                ref = OG.snapshot(_np(pool0[l, r, h]), k[h], vn[h], G[h], tr["anc"], path[r], p[-1])
+                assert _rel(_np(cyc.pool[l, r, h]), ref) < 1e-3, (r, l, h)
