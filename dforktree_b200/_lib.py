@@ -15,6 +15,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdforktree_b200.so")
 
 DFT_F32, DFT_BF16, DFT_F16 = 0, 1, 2
+DFT_OK, DFT_ERR_INVALID, DFT_ERR_UNSUPPORTED = 0, 1, 2
 DEV_BAD_TOKEN, DEV_PROBE_LIMIT, DEV_BAD_INDEX, DEV_TIMEOUT = 1, 2, 4, 8
 
 _DTYPES = {torch.float32: DFT_F32, torch.bfloat16: DFT_BF16, torch.float16: DFT_F16}

@@ -48,6 +48,70 @@ __device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v
 
 inline bool valid_dtype(int d) { return d == DFT_F32 || d == DFT_BF16 || d == DFT_F16; }
 
+// ---------------------------------------------------------------- SiLU --
+// silu(x) = x / (1 + e^-x) with e^-x = 2^(-x log2 e) from the hardware
+// base-2 exponential and 1 / d from the hardware reciprocal (both the
+// documented .approx PTX forms).  The standalone tree conv and the conv fused
+// into the tensor-core verifier share this exact sequence (the packed form
+// below rounds each lane identically), so both give bit-identical y.
+constexpr float kNegLog2e = -1.4426950408889634f;
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float silu_hw(float x) {
+  const float e = ex2_approx(__fmul_rn(x, kNegLog2e));
+  return __fmul_rn(x, rcp_approx(__fadd_rn(1.f, e)));
+}
+
+// ------------------------------------------ packed fp32 pairs (sm_100a) --
+// add / mul .rn.f32x2 round each lane exactly like the scalar .rn forms.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pk2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(f32x2 v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// two bf16 (low half = first element) <-> fp32 pair
+__device__ __forceinline__ f32x2 bf16x2_to_f32x2(uint32_t v) {
+  return pk2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2(f32x2 v) {
+  float lo, hi;
+  upk2(v, lo, hi);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ f32x2 silu_hw2(f32x2 x) {
+  const f32x2 t = mul2(x, pk2(kNegLog2e, kNegLog2e));
+  float t0, t1;
+  upk2(t, t0, t1);
+  const f32x2 d = add2(pk2(1.f, 1.f), pk2(ex2_approx(t0), ex2_approx(t1)));
+  float d0, d1;
+  upk2(d, d0, d1);
+  return mul2(x, pk2(rcp_approx(d0), rcp_approx(d1)));
+}
+
 // ------------------------------------------------------------ status word --
 __device__ __forceinline__ void raise_status(int32_t* st, int bits) {
   if (st) atomicOr(st, bits);

@@ -36,9 +36,9 @@ __global__ void tree_conv_kernel(dft_conv_args a, int32_t* st) {
       store_any(a.iw, a.iw_dtype, dst * a.iw_sd + (int64_t)n * a.iw_sn + (int64_t)c * a.iw_sc + (j - 1) * a.iw_sj, v);
   }
   if (a.bias) acc = __fadd_rn(acc, load_any(a.bias, a.w_dtype, c));
-  // SiLU with the hardware exp2 / divide (same arithmetic as the conv fused into
-  // the tcgen05 verifier, so both produce identical y)
-  const float y = __fdividef(acc, 1.f + __expf(-acc));
+  // SiLU with the hardware exp2 / reciprocal (same arithmetic as the conv fused
+  // into the tcgen05 verifier, so both produce identical y)
+  const float y = silu_hw(acc);
   store_any(a.y, a.y_dtype, (int64_t)b * a.y_sb + (int64_t)n * a.y_sn + c, y);
 }
 

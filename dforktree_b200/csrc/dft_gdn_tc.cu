@@ -5,23 +5,28 @@
 // through HBM; the tree conv (fc1_conv.py:8-27) is a fourth launch.
 //
 // Here: one persistent CTA per SM loops over work units (request, k-head);
-// a unit covers the R v-heads sharing that k-head.  Per unit:
-//   A  the unit's activation tile (pre-conv x, or y) arrives by TMA, issued
-//      at the end of the previous unit; tree conv + L2 norm in registers (one
-//      thread per channel), k/q to a swizzled operand tile B = [k; q] (tf32),
-//      gates and ancestor masks
+// a unit covers the R <= 2 v-heads sharing that k-head, and both heads run
+// side by side on disjoint warps and buffers.  Per unit:
+//   F  the unit's bf16 activation tile (pre-conv x, or y) is already in
+//      shared memory (TMA, issued during the previous unit).  Tree conv in
+//      place, one thread per channel pair in packed fp32x2 arithmetic, nodes
+//      from last to first (a node's taps are its ancestors, lower indices);
+//      then one warp per node pair: L2 norms of q / k, the swizzled tf32
+//      operand [k; q] and fp32 k_hat rows (bulk-stored to aux_k); gates and
+//      ancestor masks by three other warps
 //   M0 tcgen05 MMA  D0 = [k; q] k^T          -> k.k^T and q.k^T  (TMEM)
-//   M1 tcgen05 MMA  D1_h = S0_h [k; q]^T     -> (k S0)^T, (q S0)^T per v-head,
-//      S0_h streamed HBM -> shared by TMA (128B swizzle, no multicast); the
-//      next unit's states are requested as soon as both M1 have retired
+//   M1 tcgen05 MMA  D1_h = S0_h [k; q]^T     -> (k S0)^T, (q S0)^T per v-head;
+//      the heads' states share one 64 KB slot, streamed HBM -> shared by TMA
+//      (128B swizzle, no multicast): head 1's load is issued as soon as head
+//      0's M1 retires, the next unit's head 0 once every M1 has retired
 //   C  per v-head: A = strict-anc(beta k.k^T e^{G_i-G_j}), X = (I + A)^-1 by
-//      forward substitution, Z = (q.k^T . D) X  -> operand tile [X; Z]
+//      forward substitution, Z = (q.k^T . D) X  -> operand tile [X; Z] (3xTF32
+//      hi / lo), written over [k; q] once every M1 has retired
 //   E1 R = beta (v - e^G (k S0)) by the thread owning TMEM lane v -> R^T tile
 //   M2 tcgen05 MMA  D2_h = R^T [X; Z]^T (3xTF32) -> vn^T and (Z R)^T
-//   E2 o = e^G (q S0) + Z R, vn, G stored
-// Output tiles (k_hat, vn, o) are staged in shared memory and written with
-// bulk async copies, one per row or tile.  The state is read once, at
-// tensor-core rate, and everything else stays on chip.  Every wait is bounded (~1 s); on timeout the CTA raises
+//   E2 o = e^G (q S0) + Z R and vn staged in shared memory, bulk-stored
+// The state is read once, at tensor-core rate, and everything else stays on
+// chip.  Every wait is bounded (~1 s); on timeout the CTA raises
 // DFT_DEV_TIMEOUT, drains what it issued (bounded), frees TMEM and exits.
 #include "dft_common.cuh"
 
@@ -37,33 +42,33 @@ namespace {
 constexpr int kD = 128;
 constexpr int kNP = 32;            // nodes per tree, padded
 constexpr int kThreads = 512;
-constexpr uint32_t kTmemCols = 256;   // [0,32) k.k^T|q.k^T, [32,160) (kS0|qS0) per v-head, [160,224) vn|ZR
+constexpr uint32_t kTmemCols = 512;
+// TMEM columns: [0,32) k.k^T (lanes 0-31) | q.k^T (lanes 32-63); v-head h:
+// [32 + 64h, 96 + 64h) (k S0)^T | (q S0)^T and [160 + 64h, 224 + 64h) vn^T | (Z R)^T
+constexpr uint32_t COL_M0 = 0, COL_M1 = 32, COL_M2 = 160;
 
 // shared memory map (from a 1024-byte aligned base)
-constexpr uint32_t kS0Bytes = 64 * 1024;                 // one state tile: 4 K-blocks [128 x 128 B]
-constexpr uint32_t OFF_S0 = 0;                           // R state tiles (TMA)
-// B region (32 KB): activation tile (bf16) | [k; q] operand (4 K-blocks [64 x 128 B]) |
-//                   R^T hi, lo | output staging (vn 16 KB, o)
-constexpr uint32_t OFF_BOP = 2 * kS0Bytes;
-// U region (32 KB): second half of an fp32 activation tile | k_hat staging |
-//                   A, PD, X, [X;Z] hi, [X;Z] lo
-constexpr uint32_t OFF_UNI = OFF_BOP + 32 * 1024;
-constexpr uint32_t U_A = 0, U_PD = 4096, U_X = 8192, U_XZH = 16384, U_XZL = 24576;
-constexpr uint32_t OFF_SMALL = OFF_UNI + 32 * 1024;
+constexpr uint32_t kS0Bytes = 64 * 1024;   // one state tile: 4 K-blocks [128 x 128 B]
+constexpr uint32_t OFF_S0 = 0;
+constexpr uint32_t OFF_KQ = 64 * 1024;     // [k; q] operand (4 K-blocks [64 x 128 B]); then [X; Z] hi, lo of head h at +16 KB h
+constexpr uint32_t OFF_RT = 96 * 1024;     // head h at +32 KB h: R^T hi, lo (16 KB each), then vn | o staging
+                                           // (head 1's region stages k_hat first)
+constexpr uint32_t OFF_U = 160 * 1024;     // head h at +12 KB h: A, PD, X (4 KB each)
+constexpr uint32_t U_A = 0, U_PD = 4096, U_X = 8192, kUHead = 12288;
+constexpr uint32_t OFF_SMALL = 184 * 1024;
 constexpr uint32_t kSmallBytes = 4096;
-constexpr uint32_t kSmemBytes = OFF_SMALL + kSmallBytes + 1024;   // + alignment slack
+constexpr uint32_t OFF_ACT = 188 * 1024;   // (2 + R) parts x (conv rows + 32 node rows) x 128 bf16 channels
+constexpr uint32_t kMaxSmem = 227 * 1024;
 
 struct Small {
-  unsigned long long bar_tma[2];
-  unsigned long long bar_x;
-  unsigned long long bar_mma0, bar_mma1, bar_mma2, bar_drain;
+  unsigned long long bar_s, bar_x, bar_m0, bar_m1[2], bar_m2[2], bar_dr;
   uint32_t tmem_base;
   int abort;
   uint32_t anc[kNP];               // bit j: j is i or an ancestor of i
-  int cidx[kNP][3];                // conv columns of taps 0..2 (tap 3 is the node)
-  float norm[2][4][kNP];           // per-warp partial sums of squares of q / k rows
-  float rn[2][kNP];                // 1 / sqrt(sum + 1e-6) of q / k rows
-  float G[2][kNP], beta[2][kNP], eG[2][kNP];
+  uint32_t taps[kNP];              // tile rows of conv taps 0..2 (one byte each; tap 3 is the node)
+  __align__(16) float g[2][kNP];
+  __align__(16) float G[2][kNP];
+  float beta[2][kNP], eG[2][kNP];
 };
 static_assert(sizeof(Small) <= kSmallBytes, "small region");
 
@@ -88,8 +93,9 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait (~1 s of SM clock); false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait (~1 s of SM clock); false on timeout.  Not inlined: one copy
+// of the loop serves every call site (instruction-cache footprint).
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   const long long t0 = clock64();
   while (!mbar_try(bar, parity)) {
     if (clock64() - t0 > 2000000000ll) return false;
@@ -150,24 +156,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 32 TMEM lanes x 16 columns -> 16 registers per thread
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  __syncwarp();
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
 }
-// byte offset of element (row r, k in [0, 32)) in a K-major SW128 tile of 128-byte rows
-__device__ __forceinline__ uint32_t sw128_off(int r, int k) {
-  return (uint32_t)(r * 128 + ((((k >> 2) ^ (r & 7)) << 4) | ((k & 3) << 2)));
-}
-
-struct TcArgs {
-  dft_gdn_args g;
-  dft_gdn_conv_args cv;
-  int has_conv;
-  int R;
-  int vn_rows;     // 1: vn rows are 128 floats apart (one bulk copy per tile)
-  int k_rows;      // 1: k_hat rows are 128 floats apart
-};
 
 __device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc), "r"(bytes)
@@ -189,67 +196,107 @@ __device__ __forceinline__ void named_bar(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// anc row n of request b as a bit mask (bit j: j is n or an ancestor of n)
-__device__ __forceinline__ uint32_t anc_mask(const float* anc, int b, int n, int N) {
-  uint32_t m = 0;
-  if (n >= N) return 0;
-  const float* row = anc + ((int64_t)b * N + n) * N;
-  if (N == kNP && (((uintptr_t)row) & 15) == 0) {
-    float4 v[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) v[q] = __ldg(reinterpret_cast<const float4*>(row) + q);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      m |= (v[q].x > 0.5f ? 1u : 0u) << (4 * q);
-      m |= (v[q].y > 0.5f ? 1u : 0u) << (4 * q + 1);
-      m |= (v[q].z > 0.5f ? 1u : 0u) << (4 * q + 2);
-      m |= (v[q].w > 0.5f ? 1u : 0u) << (4 * q + 3);
-    }
-  } else {
-    for (int j = 0; j < N; ++j)
-      if (__ldg(row + j) > 0.5f) m |= 1u << j;
-  }
-  return m;
+// raw element bits (fp32, or bf16 / f16 in the low half) and their value
+__device__ __forceinline__ uint32_t ld_bits(const void* p, int dtype, int64_t i) {
+  if (dtype == DFT_F32) return __ldg(reinterpret_cast<const uint32_t*>(p) + i);
+  return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p) + i);
+}
+__device__ __forceinline__ float bits_f32(uint32_t v, int dtype) {
+  if (dtype == DFT_F32) return __uint_as_float(v);
+  if (dtype == DFT_BF16) return __uint_as_float(v << 16);
+  return __half2float(__ushort_as_half((unsigned short)v));
 }
 
-// element (i, j) of the 32 x 32 A / PD tiles: XOR-swizzled columns so that a
-// warp writing one row per lane hits 32 different banks
-__device__ __forceinline__ int sq32(int i, int j) { return i * 32 + (j ^ i); }
+// ancestor rows of request b as bit masks (bit j: j is n or an ancestor of
+// n); lane n receives row n.  One coalesced row read per step.
+__device__ __forceinline__ uint32_t anc_mask_warp(const float* anc, int b, int N, int lane) {
+  uint32_t mine = 0;
+  const float* base = anc + (int64_t)b * N * N;
+  float v[kNP];
+#pragma unroll
+  for (int n = 0; n < kNP; ++n) v[n] = (n < N && lane < N) ? __ldg(base + (int64_t)n * N + lane) : 0.f;
+#pragma unroll
+  for (int n = 0; n < kNP; ++n) {
+    const uint32_t row = __ballot_sync(0xffffffffu, v[n] > 0.5f);
+    if (lane == n) mine = row;
+  }
+  return mine;
+}
 
-template <typename T> __device__ __forceinline__ float roundT(float x) { return to_f32(from_f32<T>(x)); }
+// element (i, j) of the 32 x 32 A / PD tiles: 16-byte chunks of a row
+// XOR-swizzled by i mod 8, so that a warp storing one row chunk per lane
+// covers all banks in the minimum number of wavefronts
+__device__ __forceinline__ int sq32(int i, int j) { return i * 32 + ((((j >> 2) ^ i) & 7) << 2) + (j & 3); }
 
-template <int R, typename T>
+
+
+struct TcArgs {
+  dft_gdn_args g;
+  dft_gdn_conv_args cv;
+  int vn_rows;     // 1: vn rows are 128 floats apart (one bulk copy per tile)
+  int k_rows;      // 1: k_hat rows are 128 floats apart
+};
+
+__device__ __forceinline__ uint32_t ld_s32(const unsigned char* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ void st_s32(unsigned char* p, uint32_t v) { *reinterpret_cast<uint32_t*>(p) = v; }
+
+// four consecutive channels of a tile row
+__device__ __forceinline__ float4 ld4(const unsigned char* p, __nv_bfloat16) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                     __uint_as_float(u.y & 0xFFFF0000u));
+}
+
+// first channel of activation part p (q, k, v of head hk*R + p - 2) of k-head hk
+__device__ __forceinline__ int part_channel(int p, int hk, int Hk, int R) {
+  const int KD = Hk * kD;
+  return p == 0 ? hk * kD : (p == 1 ? KD + hk * kD : 2 * KD + (hk * R + p - 2) * kD);
+}
+
+template <int R, bool CONV>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_verify_tc(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ CUtensorMap act_map,
                   const TcArgs ta, int32_t* status) {
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  using T = __nv_bfloat16;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte aligned base, offset within the shared array (keeps the shared
+  // address space visible to the compiler: LDS / STS rather than generic access)
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
   Small& sm = *reinterpret_cast<Small*>(smem + OFF_SMALL);
+  unsigned char* act = smem + OFF_ACT;
   const dft_gdn_args& a = ta.g;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int N = a.N, Hk = a.Hk;
-  const int KD = Hk * kD;
   const int units = a.B * Hk;
-  constexpr uint32_t kBox = kNP * kD * sizeof(T);       // one activation box: 32 rows x 128 channels
-  const uint32_t bar_tma0 = smem_u32(&sm.bar_tma[0]), bar_tma1 = smem_u32(&sm.bar_tma[1]);
-  const uint32_t bar_x = smem_u32(&sm.bar_x);
-  const uint32_t bar_m0 = smem_u32(&sm.bar_mma0), bar_m1 = smem_u32(&sm.bar_mma1), bar_m2 = smem_u32(&sm.bar_mma2);
-  const uint32_t bar_dr = smem_u32(&sm.bar_drain);
-  // one control thread issues every TMA and MMA; it sits in the last warp, whose
-  // other lanes run no warp-collective tcgen05 op while it waits on a copy
+  constexpr int kOff = CONV ? 3 : 0;                   // conv-state rows ahead of the node rows
+  constexpr int kRowB = kD * 2;                        // bytes per tile row
+  constexpr int kPartB = (kOff + kNP) * kRowB;         // bytes per activation part
+  constexpr uint32_t kBox = kNP * kRowB;               // one TMA box: 32 node rows
+  const uint32_t bar_s = smem_u32(&sm.bar_s), bar_x = smem_u32(&sm.bar_x);
+  const uint32_t bar_m0 = smem_u32(&sm.bar_m0), bar_dr = smem_u32(&sm.bar_dr);
+  const uint32_t bar_m1[2] = {smem_u32(&sm.bar_m1[0]), smem_u32(&sm.bar_m1[1])};
+  const uint32_t bar_m2[2] = {smem_u32(&sm.bar_m2[0]), smem_u32(&sm.bar_m2[1])};
+  // lane 0 of the last warp issues every TMA and MMA; the warp reconverges
+  // (__syncwarp) after each control block, so that every CTA barrier is
+  // reached by whole warps
   const bool ctl = tid == kThreads - 32;
+  const bool ctl_warp = warp == kThreads / 32 - 1;
 
-  if (ctl) {
-    mbar_init(bar_tma0, 1);
-    mbar_init(bar_tma1, 1);
-    mbar_init(bar_x, 1);
-    mbar_init(bar_m0, 1);
-    mbar_init(bar_m1, 1);
-    mbar_init(bar_m2, 1);
-    mbar_init(bar_dr, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    sm.abort = 0;
+  if (ctl_warp) {
+    if (lane == 0) {
+      mbar_init(bar_s, 1);
+      mbar_init(bar_x, 1);
+      mbar_init(bar_m0, 1);
+      mbar_init(bar_m1[0], 1);
+      mbar_init(bar_m1[1], 1);
+      mbar_init(bar_m2[0], 1);
+      mbar_init(bar_m2[1], 1);
+      mbar_init(bar_dr, 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      sm.abort = 0;
+    }
+    __syncwarp();   // the control warp reconverges before the next CTA barrier
   }
   if (warp == 0) {
     __syncwarp();
@@ -262,191 +309,216 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  auto slot_of = [&](int b) -> int {
-    long long s = a.state_slots ? a.state_slots[b] : b;
-    return s < 0 ? 0 : (int)s;
-  };
-  // both v-heads' states of unit u
-  auto issue_states = [&](int u) {
-    const int b = u / Hk, hk = u % Hk, slot = slot_of(b);
+  // state of v-head hl of unit u into the slot
+  auto issue_state = [&](int u, int hl) {
+    const int b = u / Hk, hk = u % Hk;
+    const long long s = a.state_slots ? a.state_slots[b] : b;
+    const int slot = s < 0 ? 0 : (int)s;
+    mbar_expect_tx(bar_s, kS0Bytes);
 #pragma unroll
-    for (int hl = 0; hl < R; ++hl) {
-      const uint32_t bar = hl ? bar_tma1 : bar_tma0;
-      mbar_expect_tx(bar, kS0Bytes);
-#pragma unroll
-      for (int kb = 0; kb < 4; ++kb)
-        tma_load_4d(sbase + OFF_S0 + hl * kS0Bytes + kb * 16384, &pool_map, 32 * kb, 0, hk * R + hl, slot, bar);
-    }
+    for (int kb = 0; kb < 4; ++kb)
+      tma_load_4d(sbase + OFF_S0 + kb * 16384, &pool_map, 32 * kb, 0, hk * R + hl, slot, bar_s);
   };
-  // the unit's activation tile: q, k and R v column blocks x 32 rows
+  // the unit's activation tile: q, k and R v column blocks x 32 node rows
   auto issue_act = [&](int u) {
     const int b = u / Hk, hk = u % Hk;
     mbar_expect_tx(bar_x, (2 + R) * kBox);
-    tma_load_3d(sbase + OFF_BOP, &act_map, hk * kD, 0, b, bar_x);
-    tma_load_3d(sbase + OFF_BOP + kBox, &act_map, KD + hk * kD, 0, b, bar_x);
 #pragma unroll
-    for (int hl = 0; hl < R; ++hl)
-      tma_load_3d(sbase + OFF_BOP + (2 + hl) * kBox, &act_map, 2 * KD + (hk * R + hl) * kD, 0, b, bar_x);
+    for (int p = 0; p < 2 + R; ++p)
+      tma_load_3d(sbase + OFF_ACT + p * kPartB + kOff * kRowB, &act_map, part_channel(p, hk, Hk, R), 0, b, bar_x);
   };
-  int tma_pending = 0, tma_parity = 0;   // control thread: states requested but not yet consumed
-  int x_pending = 0;
-  if (ctl && (int)blockIdx.x < units) {
-    issue_states(blockIdx.x);
-    issue_act(blockIdx.x);
-    tma_pending = 1;
-    x_pending = 1;
+  // control-thread bookkeeping for the drain on timeout
+  int s_issued = 0, s_used = 0, x_issued = 0, x_used = 0;
+  if (ctl_warp) {
+    if (lane == 0 && (int)blockIdx.x < units) {
+      issue_state(blockIdx.x, 0);
+      issue_act(blockIdx.x);
+      s_issued = 1;
+      x_issued = 1;
+    }
+    __syncwarp();   // the control warp reconverges before the next CTA barrier
   }
 
-  // thread -> channel: t < 128 q, t < 256 k, then v of head (t - 256) / 128
-  const int part = tid >> 7;
-  const int d = tid & 127;
-  const bool active = part < 2 + R;
+  // conv: thread -> channel pair (part tid / 64, channels 2 (tid % 64) + {0, 1});
+  // its weights, bias and conv state are fetched one unit ahead (raw bits)
+  const int cpart = tid >> 6;
+  const int cpair = (tid & 63) * 2;
+  const bool conv_thr = CONV && tid < 64 * (2 + R);
+  uint4 pw = make_uint4(0u, 0u, 0u, 0u);
+  uint32_t pb = 0u;
+  unsigned short ps[6] = {0, 0, 0, 0, 0, 0};   // conv state (tap j, channel e) at 2 j + e
+  auto load_conv = [&](int u) {
+    const dft_gdn_conv_args& cv = ta.cv;
+    const int b = u / Hk, hk = u % Hk;
+    const int col = part_channel(cpart, hk, Hk, R) + cpair;
+    // bf16 weights [C][4]: channels col, col + 1 are 16 contiguous bytes
+    pw = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(cv.weight) + (int64_t)col * 4));
+    pb = cv.bias ? __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(cv.bias) + col)) : 0u;
+    const long long cslot = cv.conv_slots ? cv.conv_slots[b] : b;
+    const uint16_t* cs = reinterpret_cast<const uint16_t*>(cv.conv_state);
+    const int64_t c0 = cslot * cv.cs_ss + (int64_t)col * cv.cs_sc, c1 = c0 + cv.cs_sc;
+    // raw loads only: nothing here waits for them (they are consumed a unit later)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      ps[2 * j] = __ldg(cs + c0 + j * cv.cs_st);
+      ps[2 * j + 1] = __ldg(cs + c1 + j * cv.cs_st);
+    }
+  };
+  if (conv_thr && (int)blockIdx.x < units) load_conv(blockIdx.x);
+
   int it = 0;
   for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
     const int b = u / Hk, hk = u % Hk;
     const uint32_t ph = it & 1;
-    int col = 0;
-    if (part == 0) col = hk * kD + d;
-    else if (part == 1) col = KD + hk * kD + d;
-    else col = 2 * KD + (hk * R + (part - 2)) * kD + d;
-    // ------------------------------------------------ A0: per-node setup (warps 14, 15)
-    float st0 = 0.f, st1 = 0.f, st2 = 0.f, bias = 0.f, w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f;
-    if (active && ta.has_conv) {
-      const dft_gdn_conv_args& cv = ta.cv;
-      const long long cslot = cv.conv_slots ? cv.conv_slots[b] : b;
-      const int64_t cb = cslot * cv.cs_ss + (int64_t)col * cv.cs_sc;
-      st0 = load_any(cv.conv_state, cv.cs_dtype, cb);
-      st1 = load_any(cv.conv_state, cv.cs_dtype, cb + cv.cs_st);
-      st2 = load_any(cv.conv_state, cv.cs_dtype, cb + 2 * cv.cs_st);
-      w0 = load_any(cv.weight, cv.w_dtype, (int64_t)col * 4);
-      w1 = load_any(cv.weight, cv.w_dtype, (int64_t)col * 4 + 1);
-      w2 = load_any(cv.weight, cv.w_dtype, (int64_t)col * 4 + 2);
-      w3 = load_any(cv.weight, cv.w_dtype, (int64_t)col * 4 + 3);
-      bias = cv.bias ? load_any(cv.bias, cv.w_dtype, col) : 0.f;
-    }
-    if (warp == 15) {
+    // ------------------------------------------------ F0: masks and gates (before the tile lands)
+    if (warp >= 13) {
+      // warp 15: ancestor masks and conv taps; warps 13, 14: gates of v-head warp - 13
       const int n = lane;
-      sm.anc[n] = anc_mask(a.anc, b, n, N);
-      if (ta.has_conv) {
+      const uint32_t m = anc_mask_warp(a.anc, b, N, lane);
+      if (warp == 15) {
+        sm.anc[n] = m;
+        if (CONV) {
+          uint32_t packed = 0;
+          if (n < N) {
+            const int64_t* ci = ta.cv.cidx + ((int64_t)b * N + n) * 4;
 #pragma unroll
-        for (int j = 0; j < 3; ++j) {
-          long long c = n < N ? ta.cv.cidx[((int64_t)b * N + n) * 4 + j] : 3 + n;
-          if (c < 0 || c >= 3 + N) {
-            if (n < N) raise_status(status, DFT_DEV_BAD_INDEX);
-            c = 3 + n;
+            for (int j = 0; j < 3; ++j) {
+              int64_t c = ci[j];
+              if (c < 0 || c >= 3 + N) {
+                raise_status(status, DFT_DEV_BAD_INDEX);
+                c = 3 + n;
+              }
+              packed |= (uint32_t)c << (8 * j);
+            }
+            if (ci[3] != 3 + n) raise_status(status, DFT_DEV_BAD_INDEX);   // tap 3 is the node itself
           }
-          sm.cidx[n][j] = (int)c;
+          sm.taps[n] = packed;
         }
-        const long long c3 = n < N ? ta.cv.cidx[((int64_t)b * N + n) * 4 + 3] : 3 + n;
-        if (n < N && c3 != 3 + n) raise_status(status, DFT_DEV_BAD_INDEX);   // tap 3 is the node itself
-      }
-    } else if (warp == 14) {
-      // gates of the R v-heads: g, beta, G = sum over ancestors (tree_kernels.py:146-153)
-      const int n = lane;
-      const uint32_t m = anc_mask(a.anc, b, n, N);
-#pragma unroll
-      for (int hl = 0; hl < R; ++hl) {
-        const int h = hk * R + hl;
+      } else if (warp - 13 < R) {
+        // g, beta, G = sum of g over the ancestors in ascending order (tree_kernels.py:146-153)
+        const int hl = warp - 13, h = hk * R + hl;
         float g = 0.f, beta = 0.f;
         if (n < N) {
+          // raw loads first, conversions after (one memory round trip)
           const int64_t ab = (int64_t)b * a.ab_sb + (int64_t)n * a.ab_sn + h;
-          const float ar = load_any(a.a, a.ab_dtype, ab) + load_any(a.dt_bias, a.dtb_dtype, h);
+          const uint32_t ra = ld_bits(a.a, a.ab_dtype, ab), rb = ld_bits(a.bg, a.ab_dtype, ab);
+          const uint32_t rd = ld_bits(a.dt_bias, a.dtb_dtype, h);
+          const float dec = a.neg_exp_A ? __ldg(a.neg_exp_A + h) : -expf(__ldg(a.A_log + h));
+          const float ar = bits_f32(ra, a.ab_dtype) + bits_f32(rd, a.dtb_dtype);
           const float sp = ar > 20.f ? ar : logf(1.f + expf(fminf(ar, 20.f)));
-          const float dec = a.neg_exp_A ? a.neg_exp_A[h] : -expf(a.A_log[h]);
           g = dec * sp;
-          beta = 1.f / (1.f + expf(-load_any(a.bg, a.ab_dtype, ab)));
+          beta = 1.f / (1.f + expf(-bits_f32(rb, a.ab_dtype)));
         }
+        sm.g[hl][n] = g;
+        __syncwarp();
         float G = 0.f;
-#pragma unroll
-        for (int j = 0; j < kNP; ++j) {
-          const float gj = __shfl_sync(0xffffffffu, g, j);
-          if ((m >> j) & 1u) G += gj;
-        }
+        for (uint32_t mm = m; mm; mm &= mm - 1) G += sm.g[hl][__ffs(mm) - 1];
         sm.G[hl][n] = G;
         sm.beta[hl][n] = beta;
         sm.eG[hl][n] = expf(G);
         if (a.aux_g && n < N) a.aux_g[(int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh + n] = G;
       }
+      __syncwarp();
     }
-    // the activation tile (requested at the end of the previous unit)
+    // ------------------------------------------------ F1: the activation tile
     if (!mbar_wait(bar_x, ph)) atomicExch(&sm.abort, 1);
-    if (ctl) x_pending = 0;
+    if (ctl) ++x_used;
+    __syncwarp();
     __syncthreads();
     if (sm.abort) break;
-    // ------------------------------------------------ A1: tree conv (thread = channel)
-    float yv[kNP];
-    if (active) {
-      const T* tile = reinterpret_cast<const T*>(smem + OFF_BOP + part * kBox) + d;   // [n][128]
-      if (ta.has_conv) {
+    // ------------------------------------------------ F2: tree conv in place (fc1_conv.py:8-27)
+    if (conv_thr) {
+      const f32x2 w0 = pk2(__uint_as_float(pw.x << 16), __uint_as_float(pw.z << 16));
+      const f32x2 w1 = pk2(__uint_as_float(pw.x & 0xFFFF0000u), __uint_as_float(pw.z & 0xFFFF0000u));
+      const f32x2 w2 = pk2(__uint_as_float(pw.y << 16), __uint_as_float(pw.w << 16));
+      const f32x2 w3 = pk2(__uint_as_float(pw.y & 0xFFFF0000u), __uint_as_float(pw.w & 0xFFFF0000u));
+      const f32x2 bias2 = bf16x2_to_f32x2(pb);
+      const bool has_bias = ta.cv.bias != nullptr;
+      unsigned char* colp = act + cpart * kPartB + cpair * 2;   // this thread's channel pair, row 0
 #pragma unroll
-        for (int n = 0; n < kNP; ++n) {
-          float tap[3];
+      for (int j = 0; j < 3; ++j) st_s32(colp + j * kRowB, (uint32_t)ps[2 * j] | ((uint32_t)ps[2 * j + 1] << 16));
+      {
+        const int nu = u + gridDim.x;
+        if (nu < units) load_conv(nu);   // in flight until the next unit's conv
+      }
+      // one node: products and sums rounded in order j = 0..3 (fc1_conv.py:20),
+      // bias, SiLU, rounded to bf16
+      auto node = [&](uint32_t tp, int n) -> f32x2 {
+        const f32x2 x0 = bf16x2_to_f32x2(ld_s32(colp + (int)(tp & 0xFFu) * kRowB));
+        const f32x2 x1 = bf16x2_to_f32x2(ld_s32(colp + (int)((tp >> 8) & 0xFFu) * kRowB));
+        const f32x2 x2 = bf16x2_to_f32x2(ld_s32(colp + (int)((tp >> 16) & 0xFFu) * kRowB));
+        const f32x2 x3 = bf16x2_to_f32x2(ld_s32(colp + (3 + n) * kRowB));
+        f32x2 acc = mul2(x0, w0);
+        acc = add2(acc, mul2(x1, w1));
+        acc = add2(acc, mul2(x2, w2));
+        acc = add2(acc, mul2(x3, w3));
+        if (has_bias) acc = add2(acc, bias2);
+        return silu_hw2(acc);
+      };
+      int n = N - 1;
+#pragma unroll 1
+      for (; n >= 3; n -= 4) {
+        // all four nodes read their taps before any writes (a lower one may be a tap)
+        const f32x2 ya = node(sm.taps[n], n);
+        const f32x2 yb = node(sm.taps[n - 1], n - 1);
+        const f32x2 yc = node(sm.taps[n - 2], n - 2);
+        const f32x2 yd = node(sm.taps[n - 3], n - 3);
+        st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(ya));
+        st_s32(colp + (2 + n) * kRowB, f32x2_to_bf16x2(yb));
+        st_s32(colp + (1 + n) * kRowB, f32x2_to_bf16x2(yc));
+        st_s32(colp + n * kRowB, f32x2_to_bf16x2(yd));
+      }
+#pragma unroll 1
+      for (; n >= 0; --n) st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(node(sm.taps[n], n)));
+    }
+    if (CONV) __syncthreads();
+    // ------------------------------------------------ F3: norms, [k; q] operand, k_hat rows
+    {
+      // warp w: nodes w and w + 16, q and k, as four independent chains
+      float* kst = reinterpret_cast<float*>(smem + OFF_RT + 32768);   // k_hat staging [n][128] fp32
+      const int kb = lane >> 3, ch = lane & 7;                         // K-block, 16-byte chunk of channels 4 lane..
+      float4 v[2][2];
+      float ss[2][2];
 #pragma unroll
-          for (int j = 0; j < 3; ++j) {
-            const int c = sm.cidx[n][j];
-            tap[j] = c < 3 ? (c == 0 ? st0 : (c == 1 ? st1 : st2)) : to_f32(tile[(c - 3) * kD]);
-          }
-          // fc1_conv.py:20 rounds each product and sum in order j = 0..3
-          float acc = __fmul_rn(tap[0], w0);
-          acc = __fadd_rn(acc, __fmul_rn(tap[1], w1));
-          acc = __fadd_rn(acc, __fmul_rn(tap[2], w2));
-          acc = __fadd_rn(acc, __fmul_rn(to_f32(tile[n * kD]), w3));
-          acc = __fadd_rn(acc, bias);
-          // SiLU, then the reference stores y in x's dtype before the verifier reads it
-          const float yy = roundT<T>(__fdividef(acc, 1.f + __expf(-acc)));
-          yv[n] = n < N ? yy : 0.f;
+      for (int r = 0; r < 2; ++r) {
+        const int n = warp + 16 * r;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          v[r][p] = n < N ? ld4(act + p * kPartB + (kOff + n) * kRowB + lane * 8, T()) : make_float4(0.f, 0.f, 0.f, 0.f);
+          ss[r][p] = (v[r][p].x * v[r][p].x + v[r][p].y * v[r][p].y) + (v[r][p].z * v[r][p].z + v[r][p].w * v[r][p].w);
         }
-      } else {
-#pragma unroll
-        for (int n = 0; n < kNP; ++n) yv[n] = to_f32(tile[n * kD]);
       }
-    } else {
 #pragma unroll
-      for (int n = 0; n < kNP; ++n) yv[n] = 0.f;
-    }
-    // ------------------------------------------------ A2: q/k row norms
-    if (part < 2) {
+      for (int o = 16; o >= 1; o >>= 1) {
 #pragma unroll
-      for (int n = 0; n < kNP; ++n) {
-        const float s = warp_sum(yv[n] * yv[n]);
-        if (lane == 0) sm.norm[part][warp & 3][n] = s;
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int p = 0; p < 2; ++p) ss[r][p] += __shfl_xor_sync(0xffffffffu, ss[r][p], o);
       }
-    }
-    __syncthreads();   // also: every thread is done reading the activation tile
-    if (tid < 2 * kNP) {
-      const int pp = tid >> 5, n = tid & 31;
-      const float ss = (sm.norm[pp][0][n] + sm.norm[pp][1][n]) + (sm.norm[pp][2][n] + sm.norm[pp][3][n]);
-      sm.rn[pp][n] = 1.f / sqrtf(ss + 1e-6f);   // tree_kernels.py:144-145
-    }
-    __syncthreads();
-    // ------------------------------------------------ A3: k -> rows 0..31, q -> rows 32..63 (tf32); k_hat staged
-    if (part < 2) {
-      const int kb = d >> 5, kk = d & 31;
-      unsigned char* bop = smem + OFF_BOP + kb * 8192;
-      float* kst = reinterpret_cast<float*>(smem + OFF_UNI) + d;   // k_hat staging [n][128]
 #pragma unroll
-      for (int n = 0; n < kNP; ++n) {
-        float v = yv[n] * sm.rn[part][n];
-        if (part == 0) v = v * a.scale;
-        *reinterpret_cast<float*>(bop + sw128_off(part == 0 ? 32 + n : n, kk)) = tf32_rna(v);
-        if (part == 1) kst[n * kD] = v;
-      }
-      if (part == 1 && a.aux_k) {
-        fence_async_smem();
-        named_bar(3, 128);
-        if (d < 32) {
-          // lane n of the first k warp writes row n (or the whole tile when rows are contiguous)
-          const int n = d;
-          const int heads = a.aux_k_per_v ? R : 1;
-          for (int hh = 0; hh < heads; ++hh) {
-            float* g = a.aux_k + (int64_t)b * a.ak_sb + (int64_t)(a.aux_k_per_v ? hk * R + hh : hk) * a.ak_sh;
-            if (ta.k_rows) {
-              if (n == 0) bulk_store(g, smem_u32(kst - d), N * kD * 4);
-            } else if (n < N) {
-              bulk_store(g + (int64_t)n * a.ak_sn, smem_u32(kst - d + n * kD), kD * 4);
+      for (int r = 0; r < 2; ++r) {
+        const int n = warp + 16 * r;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          float4 y = v[r][p];
+          if (n < N) {
+            const float rn = 1.f / sqrtf(ss[r][p] + 1e-6f);   // tree_kernels.py:144-145
+            y.x *= rn;
+            y.y *= rn;
+            y.z *= rn;
+            y.w *= rn;
+            if (p == 0) {
+              y.x *= a.scale;
+              y.y *= a.scale;
+              y.z *= a.scale;
+              y.w *= a.scale;
+            } else {
+              *reinterpret_cast<float4*>(kst + n * kD + lane * 4) = y;
             }
           }
-          bulk_commit_and_wait_read();
+          const int row = p == 0 ? 32 + n : n;   // k rows 0..31, q rows 32..63
+          const float4 t = make_float4(tf32_rna(y.x), tf32_rna(y.y), tf32_rna(y.z), tf32_rna(y.w));
+          *reinterpret_cast<float4*>(smem + OFF_KQ + kb * 8192 + row * 128 + ((ch ^ (row & 7)) << 4)) = t;
         }
       }
     }
@@ -454,240 +526,280 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // ------------------------------------------------ M0, M1 (one thread issues)
-    if (ctl) {
-      const uint32_t id0 = idesc_tf32(128, 32), id1 = idesc_tf32(128, 64);
-#pragma unroll
-      for (int kb = 0; kb < 4; ++kb) {
-        const uint64_t db = sw128_desc(sbase + OFF_BOP + kb * 8192);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + 0, db + 2 * ks, db + 2 * ks, id0, (kb | ks) != 0);
-      }
-      mma_commit(bar_m0);
-#pragma unroll
-      for (int hl = 0; hl < R; ++hl) {
-        if (!mbar_wait(hl ? bar_tma1 : bar_tma0, ph)) {
-          atomicExch(&sm.abort, 1);
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
+    // ------------------------------------------------ M0, M1 of head 0 (one thread issues)
+    if (ctl_warp) {
+      if (lane == 0) {
+        const uint32_t id0 = idesc_tf32(128, 32), id1 = idesc_tf32(128, 64);
+  #pragma unroll 1
         for (int kb = 0; kb < 4; ++kb) {
-          const uint64_t da = sw128_desc(sbase + OFF_S0 + hl * kS0Bytes + kb * 16384);
-          const uint64_t db = sw128_desc(sbase + OFF_BOP + kb * 8192);
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            mma_tf32(tmem + 32 + 64 * hl, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
+          const uint64_t db = sw128_desc(sbase + OFF_KQ + kb * 8192);
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M0, db + 2 * ks, db + 2 * ks, id0, (kb | ks) != 0);
+        }
+        mma_commit(bar_m0);
+        if (!mbar_wait(bar_s, s_used & 1)) atomicExch(&sm.abort, 1);
+        ++s_used;
+        tc_fence_after();
+  #pragma unroll 1
+        for (int kb = 0; kb < 4; ++kb) {
+          const uint64_t da = sw128_desc(sbase + OFF_S0 + kb * 16384);
+          const uint64_t db = sw128_desc(sbase + OFF_KQ + kb * 8192);
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
+        }
+        mma_commit(bar_m1[0]);
+        if (R == 2) {
+          // head 1's state into the slot once head 0's M1 has read it
+          if (!mbar_wait(bar_m1[0], ph)) atomicExch(&sm.abort, 1);
+          issue_state(u, 1);
+          ++s_issued;
         }
       }
-      tma_pending = 0;
-      mma_commit(bar_m1);
+      __syncwarp();   // the control warp reconverges before the next CTA barrier
     }
-    // ------------------------------------------------ C + E per v-head
-    for (int hl = 0; hl < R; ++hl) {
-      // A and PD rows from k.k^T (lanes 0..31) and q.k^T (lanes 32..63)
-      if (warp < 2) {
-        if (!mbar_wait(bar_m0, ph)) atomicExch(&sm.abort, 1);
+    // k_hat rows -> aux_k (one warp; the staging is free again before head 1's E1)
+    if (warp == 8 && a.aux_k) {
+      const int heads = a.aux_k_per_v ? R : 1;
+      const float* kst = reinterpret_cast<const float*>(smem + OFF_RT + 32768);
+      for (int hh = 0; hh < heads; ++hh) {
+        float* g = a.aux_k + (int64_t)b * a.ak_sb + (int64_t)(a.aux_k_per_v ? hk * R + hh : hk) * a.ak_sh;
+        if (ta.k_rows) {
+          if (lane == 0) bulk_store(g, smem_u32(kst), N * kD * 4);
+        } else if (lane < N) {
+          bulk_store(g + (int64_t)lane * a.ak_sn, smem_u32(kst + lane * kD), kD * 4);
+        }
+      }
+      bulk_commit_and_wait_read();
+      __syncwarp();
+    }
+    // ------------------------------------------------ C1: A and PD of every head (8 warps)
+    // warp w: rows from TMEM lanes 32 (w % 4) (k.k^T for w % 4 == 0, q.k^T for 1),
+    // head (w / 4) % 2, columns 16 (w / 8) .. + 15
+    if ((warp & 3) < 2 && ((warp >> 2) & 1) < R) {
+      const int hh = (warp >> 2) & 1, half = warp >> 3;
+      const bool pd = warp & 1;
+      if (!mbar_wait(bar_m0, ph)) atomicExch(&sm.abort, 1);
+      tc_fence_after();
+      float kk[16];
+      tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + COL_M0 + 16 * half, kk);
+      // A: strict ancestors, beta_i k.k^T e^{G_i-G_j}; PD: ancestors, q.k^T e^{G_i-G_j}
+      const int i = lane;
+      const uint32_t keep = pd ? sm.anc[i] : sm.anc[i] & ~(1u << i);
+      const float Gi = sm.G[hh][i], ci = pd ? 1.f : sm.beta[hh][i];
+      float* dst = reinterpret_cast<float*>(smem + OFF_U + hh * kUHead + (pd ? U_PD : U_A));
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int j0 = 16 * half + 4 * c;
+        const float4 gj = *reinterpret_cast<const float4*>(&sm.G[hh][j0]);
+        float4 o;
+        o.x = ((keep >> j0) & 1u) ? ci * kk[4 * c] * __expf(Gi - gj.x) : 0.f;
+        o.y = ((keep >> (j0 + 1)) & 1u) ? ci * kk[4 * c + 1] * __expf(Gi - gj.y) : 0.f;
+        o.z = ((keep >> (j0 + 2)) & 1u) ? ci * kk[4 * c + 2] * __expf(Gi - gj.z) : 0.f;
+        o.w = ((keep >> (j0 + 3)) & 1u) ? ci * kk[4 * c + 3] * __expf(Gi - gj.w) : 0.f;
+        *reinterpret_cast<float4*>(dst + sq32(i, j0)) = o;
+      }
+    }
+    __syncthreads();
+    if (sm.abort) break;
+    // ------------------------------------------------ X = (I + A)^-1 per head (warps 2, 6); head 1's M1
+    if ((warp & 3) == 2 && (warp >> 2) < R) {
+      // one column per lane, kept in registers
+      const float* A = reinterpret_cast<const float*>(smem + OFF_U + (warp >> 2) * kUHead + U_A);
+      float* X = reinterpret_cast<float*>(smem + OFF_U + (warp >> 2) * kUHead + U_X);
+      const int c = lane;
+      float xc[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+        for (int m = 0; m < i; m += 4) {
+          s0 = fmaf(A[sq32(i, m)], xc[m], s0);
+          if (m + 1 < i) s1 = fmaf(A[sq32(i, m + 1)], xc[m + 1], s1);
+          if (m + 2 < i) s2 = fmaf(A[sq32(i, m + 2)], xc[m + 2], s2);
+          if (m + 3 < i) s3 = fmaf(A[sq32(i, m + 3)], xc[m + 3], s3);
+        }
+        xc[i] = (i == c ? 1.f : 0.f) - ((s0 + s1) + (s2 + s3));
+        X[i * 32 + c] = xc[i];
+      }
+    }
+    if (ctl_warp) {
+      if (R == 2 && lane == 0) {
+        if (!mbar_wait(bar_s, s_used & 1)) atomicExch(&sm.abort, 1);
+        ++s_used;
         tc_fence_after();
-        float kk[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 0, kk);
-        const int i = lane;
-        const uint32_t mi = sm.anc[i];
-        const float Gi = sm.G[hl][i], bi = sm.beta[hl][i];
-        float* dst = reinterpret_cast<float*>(smem + OFF_UNI + (warp == 0 ? U_A : U_PD));
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const bool anc = (mi >> j) & 1u;
-          const float D = anc ? __expf(Gi - sm.G[hl][j]) : 0.f;
-          dst[sq32(i, j)] = warp == 0 ? ((anc && j != i) ? bi * kk[j] * D : 0.f) : (anc ? kk[j] * D : 0.f);
+        const uint32_t id1 = idesc_tf32(128, 64);
+  #pragma unroll 1
+        for (int kb = 0; kb < 4; ++kb) {
+          const uint64_t da = sw128_desc(sbase + OFF_S0 + kb * 16384);
+          const uint64_t db = sw128_desc(sbase + OFF_KQ + kb * 8192);
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1 + 64, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
         }
+        mma_commit(bar_m1[1]);
       }
-      __syncthreads();
-      if (sm.abort) break;
-      // X = (I + A)^-1: one column per lane of warp 2, column kept in registers
-      if (warp == 2) {
-        const float* A = reinterpret_cast<const float*>(smem + OFF_UNI + U_A);
-        float* X = reinterpret_cast<float*>(smem + OFF_UNI + U_X);
-        const int c = lane;
-        float xc[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-          for (int m = 0; m < i; m += 4) {
-            s0 = fmaf(A[sq32(i, m)], xc[m], s0);
-            if (m + 1 < i) s1 = fmaf(A[sq32(i, m + 1)], xc[m + 1], s1);
-            if (m + 2 < i) s2 = fmaf(A[sq32(i, m + 2)], xc[m + 2], s2);
-            if (m + 3 < i) s3 = fmaf(A[sq32(i, m + 3)], xc[m + 3], s3);
-          }
-          xc[i] = (i == c ? 1.f : 0.f) - ((s0 + s1) + (s2 + s3));
-          X[i * 32 + c] = xc[i];
-        }
-      }
-      __syncthreads();
-      // [X; Z] operand (hi / lo tf32 split): rows 0..31 X, rows 32..63 Z = PD X
-      {
-        const float* PD = reinterpret_cast<const float*>(smem + OFF_UNI + U_PD);
-        const float* X = reinterpret_cast<const float*>(smem + OFF_UNI + U_X);
-        unsigned char* xzh = smem + OFF_UNI + U_XZH;
-        unsigned char* xzl = smem + OFF_UNI + U_XZL;
-        const int t = tid & 255, n = t >> 3, c = t & 7;   // row n, 16-byte chunk c (columns 4c..4c+3)
-        float4 v;
-        int row;
-        if (tid < 256) {
-          float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      __syncwarp();   // the control warp reconverges before the next CTA barrier
+    }
+    __syncthreads();
+    if (sm.abort) break;
+    // ------------------------------------------------ [X; Z] operands (warps 0-7) and E1 (warps 8-15)
+    if (tid < 256) {
+      // rows 0..31 X, rows 32..63 Z = PD X, hi / lo tf32 split, over [k; q] once every M1 has retired
+      if (!mbar_wait(bar_m1[R - 1], ph)) atomicExch(&sm.abort, 1);
+      const int n = tid >> 3, c = tid & 7;   // row n, 16-byte chunk c (columns 4c..4c+3)
+#pragma unroll 1
+      for (int hh = 0; hh < R; ++hh) {
+        const float* PD = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + U_PD);
+        const float* X = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + U_X);
+        unsigned char* xzh = smem + OFF_KQ + hh * 16384;
+        unsigned char* xzl = xzh + 8192;
+        float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
-          for (int j = 0; j < 32; ++j) {
-            const float pd = PD[sq32(n, j)];
-            const float4 xr = *reinterpret_cast<const float4*>(X + j * 32 + 4 * c);
-            z.x = fmaf(pd, xr.x, z.x);
-            z.y = fmaf(pd, xr.y, z.y);
-            z.z = fmaf(pd, xr.z, z.z);
-            z.w = fmaf(pd, xr.w, z.w);
-          }
-          v = z;
-          row = 32 + n;
-        } else {
-          v = *reinterpret_cast<const float4*>(X + n * 32 + 4 * c);
-          row = n;
+        for (int j = 0; j < 32; ++j) {
+          const float pdv = PD[sq32(n, j)];
+          const float4 xr = *reinterpret_cast<const float4*>(X + j * 32 + 4 * c);
+          z.x = fmaf(pdv, xr.x, z.x);
+          z.y = fmaf(pdv, xr.y, z.y);
+          z.z = fmaf(pdv, xr.z, z.z);
+          z.w = fmaf(pdv, xr.w, z.w);
         }
-        float4 hi, lo;
-        hi.x = tf32_rna(v.x); lo.x = tf32_rna(v.x - hi.x);
-        hi.y = tf32_rna(v.y); lo.y = tf32_rna(v.y - hi.y);
-        hi.z = tf32_rna(v.z); lo.z = tf32_rna(v.z - hi.z);
-        hi.w = tf32_rna(v.w); lo.w = tf32_rna(v.w - hi.w);
-        const uint32_t off = (uint32_t)(row * 128 + ((c ^ (row & 7)) << 4));
-        *reinterpret_cast<float4*>(xzh + off) = hi;
-        *reinterpret_cast<float4*>(xzl + off) = lo;
-      }
-      // E1: R = beta (v - e^G (k S0)) by the threads of this head's v part
-      const bool epi = part == 2 + hl;
-      if (epi) {
-        if (!mbar_wait(bar_m1, ph)) atomicExch(&sm.abort, 1);
-        tc_fence_after();
-        const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 32 + 64 * hl;
-        float ks_[kNP];
-        tmem_ld32(taddr, ks_);
-        unsigned char* rth = smem + OFF_BOP;
-        unsigned char* rtl = smem + OFF_BOP + 16384;
-        const int v = d;
-        // row v of R^T: eight 16-byte chunks, swizzled (chunk c at c ^ (v & 7))
+        const float4 xv = *reinterpret_cast<const float4*>(X + n * 32 + 4 * c);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int q = 0; q < 2; ++q) {
+          const float4 v = q ? z : xv;
+          const int row = q ? 32 + n : n;
           float4 hi, lo;
-          float* phi = &hi.x;
-          float* plo = &lo.x;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int n = 4 * c + e;
-            const float rr = sm.beta[hl][n] * (yv[n] - sm.eG[hl][n] * ks_[n]);
-            phi[e] = tf32_rna(rr);
-            plo[e] = tf32_rna(rr - phi[e]);
-          }
-          const uint32_t off = (uint32_t)(v * 128 + ((c ^ (v & 7)) << 4));
-          *reinterpret_cast<float4*>(rth + off) = hi;
-          *reinterpret_cast<float4*>(rtl + off) = lo;
+          hi.x = tf32_rna(v.x); lo.x = tf32_rna(v.x - hi.x);
+          hi.y = tf32_rna(v.y); lo.y = tf32_rna(v.y - hi.y);
+          hi.z = tf32_rna(v.z); lo.z = tf32_rna(v.z - hi.z);
+          hi.w = tf32_rna(v.w); lo.w = tf32_rna(v.w - hi.w);
+          const uint32_t off = (uint32_t)(row * 128 + ((c ^ (row & 7)) << 4));
+          *reinterpret_cast<float4*>(xzh + off) = hi;
+          *reinterpret_cast<float4*>(xzl + off) = lo;
         }
       }
-      // the states of this unit are consumed: request the next unit's
-      if (ctl && hl == 0 && !sm.abort) {
-        if (!mbar_wait(bar_m1, ph)) atomicExch(&sm.abort, 1);
-        const int nu = u + gridDim.x;
-        if (nu < units && !sm.abort) {
-          issue_states(nu);
-          tma_pending = 1;
-          tma_parity = (it + 1) & 1;
+    } else if (((warp - 8) >> 2) < R) {
+      // E1: R = beta (v - e^G (k S0)) by the four warps owning head hh's TMEM lanes
+      const int hh = (warp - 8) >> 2;
+      if (!mbar_wait(bar_m1[hh], ph)) atomicExch(&sm.abort, 1);
+      tc_fence_after();
+      float ks_[kNP];
+      tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + COL_M1 + 64 * hh, ks_);
+      unsigned char* rth = smem + OFF_RT + hh * 32768;
+      unsigned char* rtl = rth + 16384;
+      const int v = tid & 127;
+      const T* yv = reinterpret_cast<const T*>(act + (2 + hh) * kPartB + kOff * kRowB) + v;
+      // row v of R^T: eight 16-byte chunks, swizzled (chunk c at c ^ (v & 7))
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float4 hi, lo;
+        float* phi = &hi.x;
+        float* plo = &lo.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = 4 * c + e;
+          const float rr = sm.beta[hh][n] * (to_f32(yv[n * kD]) - sm.eG[hh][n] * ks_[n]);
+          phi[e] = tf32_rna(rr);
+          plo[e] = tf32_rna(rr - phi[e]);
         }
+        const uint32_t off = (uint32_t)(v * 128 + ((c ^ (v & 7)) << 4));
+        *reinterpret_cast<float4*>(rth + off) = hi;
+        *reinterpret_cast<float4*>(rtl + off) = lo;
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (sm.abort) break;
+    if (ctl_warp) {
+      if (lane == 0) {
+        // every M1 of this unit has retired and the tile is consumed: request the next unit's
+        const int nu = u + gridDim.x;
+        if (nu < units) {
+          issue_state(nu, 0);
+          issue_act(nu);
+          ++s_issued;
+          ++x_issued;
+        }
+        // M2 per head: D2 = R^T [X; Z]^T, 3xTF32 (hi.hi + hi.lo + lo.hi)
+        const uint32_t id2 = idesc_tf32(128, 64);
+  #pragma unroll 1
+        for (int hh = 0; hh < R; ++hh) {
+          const uint32_t dcol = tmem + COL_M2 + 64 * hh;
+          const uint64_t ah = sw128_desc(sbase + OFF_RT + hh * 32768), al = sw128_desc(sbase + OFF_RT + hh * 32768 + 16384);
+          const uint64_t bh = sw128_desc(sbase + OFF_KQ + hh * 16384), bl = sw128_desc(sbase + OFF_KQ + hh * 16384 + 8192);
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, ah + 2 * ks, bh + 2 * ks, id2, ks != 0);
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, ah + 2 * ks, bl + 2 * ks, id2, 1);
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, al + 2 * ks, bh + 2 * ks, id2, 1);
+          mma_commit(bar_m2[hh]);
+        }
+      }
+      __syncwarp();   // the control warp reconverges before the next CTA barrier
+    }
+    // ------------------------------------------------ E2: vn and o = e^G (q S0) + Z R, bulk-stored
+    if (warp >= 8 && ((warp - 8) >> 2) < R) {
+      const int hh = (warp - 8) >> 2;
+      if (!mbar_wait(bar_m2[hh], ph)) atomicExch(&sm.abort, 1);
+      tc_fence_after();
+      const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
+      const int h = hk * R + hh, v = tid & 127;
+      float* vst = reinterpret_cast<float*>(smem + OFF_RT + hh * 32768);            // [n][128] f32, over R^T
+      T* ost = reinterpret_cast<T*>(smem + OFF_RT + hh * 32768 + 16384);            // [n][128] bf16
+      {
+        float vn[32];
+        tmem_ld32(tmem + lanes + COL_M2 + 64 * hh, vn);
+#pragma unroll
+        for (int n = 0; n < kNP; ++n) vst[n * kD + v] = vn[n];
+      }
+      {
+        float zr[32], qs[32];
+        tmem_ld32(tmem + lanes + COL_M2 + 64 * hh + 32, zr);
+        tmem_ld32(tmem + lanes + COL_M1 + 64 * hh + 32, qs);
+#pragma unroll
+        for (int n = 0; n < kNP; ++n) ost[n * kD + v] = __float2bfloat16_rn(sm.eG[hh][n] * qs[n] + zr[n]);
       }
       fence_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      if (sm.abort) break;
-      // M2: D2 = R^T [X; Z]^T, 3xTF32 (hi.hi + hi.lo + lo.hi), TMEM columns 160..223
-      if (ctl) {
-        const uint32_t id2 = idesc_tf32(128, 64);
-        const uint32_t dcol = tmem + 160;
-        const uint64_t ah = sw128_desc(sbase + OFF_BOP), al = sw128_desc(sbase + OFF_BOP + 16384);
-        const uint64_t bh = sw128_desc(sbase + OFF_UNI + U_XZH), bl = sw128_desc(sbase + OFF_UNI + U_XZL);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, ah + 2 * ks, bh + 2 * ks, id2, ks != 0);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, ah + 2 * ks, bl + 2 * ks, id2, 1);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, al + 2 * ks, bh + 2 * ks, id2, 1);
-        mma_commit(bar_m2);
-      }
-      // E2: vn and o = e^G (q S0) + Z R, staged in the (now free) B region, bulk-stored
-      if (epi) {
-        if (!mbar_wait(bar_m2, (it * R + hl) & 1)) atomicExch(&sm.abort, 1);
-        tc_fence_after();
-        const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
-        const int h = hk * R + hl, v = d;
-        float* vst = reinterpret_cast<float*>(smem + OFF_BOP);                  // [n][128] f32
-        T* ost = reinterpret_cast<T*>(smem + OFF_BOP + 16384);                  // [n][128] T
-        {
-          float vn[32];
-          tmem_ld32(tmem + lanes + 160, vn);
-#pragma unroll
-          for (int n = 0; n < kNP; ++n) vst[n * kD + v] = vn[n];
-        }
-        {
-          float zr[32], qs[32];
-          tmem_ld32(tmem + lanes + 192, zr);
-          tmem_ld32(tmem + lanes + 32 + 64 * hl + 32, qs);
-#pragma unroll
-          for (int n = 0; n < kNP; ++n) ost[n * kD + v] = from_f32<T>(sm.eG[hl][n] * qs[n] + zr[n]);
-        }
-        fence_async_smem();
-        named_bar(1 + hl, 128);
-        if (d < 32) {
-          const int n = d;
-          if (a.aux_vn) {
-            float* g = a.aux_vn + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh;
-            if (ta.vn_rows) {
-              if (n == 0) bulk_store(g, smem_u32(vst), N * kD * 4);
-            } else if (n < N) {
-              bulk_store(g + (int64_t)n * a.av_sn, smem_u32(vst + n * kD), kD * 4);
-            }
+      named_bar(1 + hh, 128);
+      if ((warp & 3) == 0) {
+        const int n = lane;
+        if (a.aux_vn) {
+          float* g = a.aux_vn + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh;
+          if (ta.vn_rows) {
+            if (n == 0) bulk_store(g, smem_u32(vst), N * kD * 4);
+          } else if (n < N) {
+            bulk_store(g + (int64_t)n * a.av_sn, smem_u32(vst + n * kD), kD * 4);
           }
-          if (n < N) {
-            T* g = reinterpret_cast<T*>(a.o) + (int64_t)b * a.o_sb + (int64_t)n * a.o_sn + (int64_t)h * a.o_sh;
-            bulk_store(g, smem_u32(ost + n * kD), kD * sizeof(T));
-          }
-          bulk_commit_and_wait_read();
         }
-      } else if (ctl) {
-        if (!mbar_wait(bar_m2, (it * R + hl) & 1)) atomicExch(&sm.abort, 1);
+        if (n < N) {
+          T* g = reinterpret_cast<T*>(a.o) + (int64_t)b * a.o_sb + (int64_t)n * a.o_sn + (int64_t)h * a.o_sh;
+          bulk_store(g, smem_u32(ost + n * kD), kD * 2);
+        }
+        bulk_commit_and_wait_read();
+        __syncwarp();
       }
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      if (sm.abort) break;
     }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
     if (sm.abort) break;
-    // the B / U regions are free again: request the next unit's activation tile
-    if (ctl) {
-      const int nu = u + gridDim.x;
-      if (nu < units) {
-        issue_act(nu);
-        x_pending = 1;
-      }
-    }
   }
   // ------------------------------------------------ teardown
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // own output copies complete
   __syncthreads();
   if (sm.abort) {
-    if (ctl) {
-      raise_status(status, DFT_DEV_TIMEOUT);
-      // drain what this CTA issued before freeing its shared memory / TMEM (bounded)
-      if (tma_pending) {
-        mbar_wait(bar_tma0, tma_parity);
-        if (R > 1) mbar_wait(bar_tma1, tma_parity);
+    if (ctl_warp) {
+      if (lane == 0) {
+        raise_status(status, DFT_DEV_TIMEOUT);
+        // drain what this CTA issued before freeing its shared memory / TMEM (bounded)
+        for (; s_used < s_issued; ++s_used) mbar_wait(bar_s, s_used & 1);
+        for (; x_used < x_issued; ++x_used) mbar_wait(bar_x, x_used & 1);
+        mma_commit(bar_dr);   // arrives once every MMA this thread issued has retired
+        mbar_wait(bar_dr, 0);
       }
-      if (x_pending) mbar_wait(bar_x, it & 1);
-      mma_commit(bar_dr);   // arrives once every MMA this thread issued has retired
-      mbar_wait(bar_dr, 0);
+      __syncwarp();   // the control warp reconverges before the next CTA barrier
     }
     __syncthreads();
   }
@@ -727,20 +839,30 @@ int sm_count() {
 
 inline bool al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+// dynamic shared memory of one launch: fixed regions + activation tile + alignment slack
+uint32_t smem_bytes(int R, bool conv) {
+  const uint32_t act = (uint32_t)(2 + R) * (uint32_t)((conv ? 3 : 0) + kNP) * kD * 2;
+  return OFF_ACT + act + 1024;
+}
+
 }  // namespace
 
 // The tcgen05 path applies for N <= 32, Dk = Dv = 128, R = Hv / Hk in {1, 2},
-// float / bfloat16 activations with o in the same dtype, a pool with unit k
-// stride and 16-byte multiple strides and a known slot count, and outputs
-// whose rows are 16-byte aligned (bulk copies).
+// bfloat16 activations and o (the fused tree conv: bfloat16 x, conv state and
+// weights), a pool with unit k stride, 16-byte multiple strides and a known
+// slot count, and 16-byte aligned output rows.
 bool dft_gdn_tc_applicable(const dft_gdn_args* a) {
   if (a->force_simt) return false;
   const int dt = a->conv ? a->conv->x_dtype : a->y_dtype;
-  if ((dt != DFT_F32 && dt != DFT_BF16) || a->o_dtype != dt) return false;
-  const int es = dt == DFT_F32 ? 4 : 2;
+  if (dt != DFT_BF16 || a->o_dtype != dt) return false;
+  if (a->conv && (a->conv->cs_dtype != DFT_BF16 || a->conv->w_dtype != DFT_BF16 ||
+                  !al16(a->conv->weight) || ((uintptr_t)a->conv->bias & 3)))
+    return false;
+  const int es = 2;
   if (a->N > kNP || a->Dk != kD || a->Dv != kD) return false;
   const int R = a->Hv / a->Hk;
   if (R != 1 && R != 2) return false;
+  if (smem_bytes(R, a->conv != nullptr) > kMaxSmem) return false;
   if (a->p_sk != 1 || a->p_nslots <= 0) return false;
   if ((a->p_sv * 4) % 16 || (a->p_sh * 4) % 16 || (a->p_ss * 4) % 16) return false;
   if (!al16(a->pool)) return false;
@@ -769,10 +891,9 @@ int dft_gdn_tc_launch(const dft_gdn_args* a, int32_t* status, cudaStream_t st) {
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return DFT_ERR_UNSUPPORTED;
   }
-  const int dt = a->conv ? a->conv->x_dtype : a->y_dtype;
-  const int es = dt == DFT_F32 ? 4 : 2;
+  const int es = 2;
   {
-    // activation (pre-conv x or y) as [B][N][C]: rows >= N of a 32-row box read as zeros
+    // activation (pre-conv x, or y) as [B][N][C]: rows >= N of a 32-row box read as zeros
     const void* act = a->conv ? a->conv->x : a->y;
     const int64_t sn = a->conv ? a->conv->x_sn : a->y_sn, sb = a->conv ? a->conv->x_sb : a->y_sb;
     const int64_t C = 2 * (int64_t)a->Hk * a->Dk + (int64_t)a->Hv * a->Dv;
@@ -780,7 +901,7 @@ int dft_gdn_tc_launch(const dft_gdn_args* a, int32_t* status, cudaStream_t st) {
     const cuuint64_t strides[2] = {(cuuint64_t)(sn * es), (cuuint64_t)(sb * es)};
     const cuuint32_t box[3] = {128, (cuuint32_t)kNP, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
-    if (encode_fn()(&act_map, dt == DFT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+    if (encode_fn()(&act_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
                     const_cast<void*>(act), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -788,23 +909,24 @@ int dft_gdn_tc_launch(const dft_gdn_args* a, int32_t* status, cudaStream_t st) {
   }
   TcArgs ta;
   ta.g = *a;
-  ta.has_conv = a->conv != nullptr;
   if (a->conv) ta.cv = *a->conv;
   else memset(&ta.cv, 0, sizeof(ta.cv));
-  ta.R = a->Hv / a->Hk;
   ta.vn_rows = a->av_sn == kD;
   ta.k_rows = a->ak_sn == kD;
+  const int R = a->Hv / a->Hk;
+  const bool conv = a->conv != nullptr;
+  const uint32_t smem = smem_bytes(R, conv);
   const int units = a->B * a->Hk;
   const int grid = units < sm_count() ? units : sm_count();
   auto go = [&](auto kernel) -> int {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return DFT_ERR_CUDA;
-    kernel<<<grid, kThreads, kSmemBytes, st>>>(pool_map, act_map, ta, status);
+    kernel<<<grid, kThreads, smem, st>>>(pool_map, act_map, ta, status);
     return DFT_OK;
   };
   int rc;
-  if (ta.R == 2) rc = dt == DFT_BF16 ? go(gdn_verify_tc<2, __nv_bfloat16>) : go(gdn_verify_tc<2, float>);
-  else rc = dt == DFT_BF16 ? go(gdn_verify_tc<1, __nv_bfloat16>) : go(gdn_verify_tc<1, float>);
+  if (conv) rc = R == 2 ? go(gdn_verify_tc<2, true>) : go(gdn_verify_tc<1, true>);
+  else rc = R == 2 ? go(gdn_verify_tc<2, false>) : go(gdn_verify_tc<1, false>);
   if (rc) return rc;
   DFT_LAUNCH_CHECK();
   return DFT_OK;

@@ -319,8 +319,18 @@ def gdn_tree_verify(y, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk=128, Dv=128, 
                      ag_sh=aux_g.stride(1) if aux_g is not None else 0,
                      conv=C.pointer(cv) if cv is not None else None, force_simt=int(bool(force_simt)))
     keep = (anc, A_log_f, neg, dtb, keep_cv, cv)
-    L.check(lib.dft_gdn_tree_verify(C.byref(args), _status_ptr(status), L.stream_handle()), "dft_gdn_tree_verify")
+    rc = lib.dft_gdn_tree_verify(C.byref(args), _status_ptr(status), L.stream_handle())
     del keep
+    if rc == L.DFT_ERR_UNSUPPORTED and conv is not None:
+        # the fused conv lives in the tensor-core path (bf16 x and conv state):
+        # otherwise run the tree conv as its own launch, then the verify
+        yc = tree_conv(conv["x"], conv["conv_state"], conv["weight"], conv.get("bias"), conv["cidx"],
+                       state_slots=conv.get("conv_slots"), status=status)
+        return gdn_tree_verify(yc, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk, Dv, state_slots=state_slots,
+                               scale=scale, neg_exp_A=neg_exp_A, o=o, aux_k=aux_k, aux_vn=aux_vn, aux_g=aux_g,
+                               aux_k_per_v=aux_k_per_v, status=status, pool_strides=pool_strides,
+                               pool_nslots=pool_nslots, force_simt=force_simt)
+    L.check(rc, "dft_gdn_tree_verify")
     return o
 
 

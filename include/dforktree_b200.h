@@ -206,7 +206,10 @@ DFT_API int dft_tree_conv(const dft_conv_args* a, int32_t* dev_status, void* str
  * the reference's CTX.keys layout) or k-head; vn (b, h, n, v); G (b, h, n).
  * With `conv` set, y is not read: the tree conv of fc1_conv.py:8-27 is
  * computed from the pre-conv inputs inside the verifier (the window taps
- * are not written; dft_tree_conv does that for the drop-in hook). */
+ * are not written; dft_tree_conv does that for the drop-in hook).  The fused
+ * conv runs on the tensor-core path only (N <= 32, Dk = Dv = 128, Hv / Hk in
+ * {1, 2}, bfloat16 x, conv state, weights and o, 16-byte aligned rows); others
+ * return DFT_ERR_UNSUPPORTED and take dft_tree_conv + this call on y. */
 typedef struct {
   const void* x; int32_t x_dtype; int64_t x_sb, x_sn;   /* pre-conv (b, n, col), col stride 1 */
   const void* conv_state; int32_t cs_dtype; int64_t cs_ss, cs_sc, cs_st;
