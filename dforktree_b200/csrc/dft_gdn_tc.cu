@@ -12,19 +12,22 @@
 //      place, one thread per channel pair in packed fp32x2 arithmetic, nodes
 //      from last to first (a node's taps are its ancestors, lower indices);
 //      then one warp per node pair: L2 norms of q / k, the swizzled tf32
-//      operand [k; q] and fp32 k_hat rows (bulk-stored to aux_k); gates and
+//      operand [k; q] and the fp32 k_hat rows (stored to aux_k); gates and
 //      ancestor masks by three other warps
 //   M0 tcgen05 MMA  D0 = [k; q] k^T          -> k.k^T and q.k^T  (TMEM)
 //   M1 tcgen05 MMA  D1_h = S0_h [k; q]^T     -> (k S0)^T, (q S0)^T per v-head;
 //      the heads' states share one 64 KB slot, streamed HBM -> shared by TMA
 //      (128B swizzle, no multicast): head 1's load is issued as soon as head
 //      0's M1 retires, the next unit's head 0 once every M1 has retired
-//   C  per v-head: A = strict-anc(beta k.k^T e^{G_i-G_j}), X = (I + A)^-1 by
-//      forward substitution, Z = (q.k^T . D) X  -> operand tile [X; Z] (3xTF32
-//      hi / lo), written over [k; q] once every M1 has retired
+//   C  per v-head: A = strict-anc(beta k.k^T e^{G_i-G_j}) and PD = q.k^T . D;
+//      X = (I + A)^-1 by forward substitution and Z = PD X by backward
+//      substitution of Z (I + A) = PD, on two warps at once -> operand tile
+//      [X; Z] (3xTF32 hi / lo), written over [k; q] once every M1 has retired
 //   E1 R = beta (v - e^G (k S0)) by the thread owning TMEM lane v -> R^T tile
+//      (alongside C's solves)
 //   M2 tcgen05 MMA  D2_h = R^T [X; Z]^T (3xTF32) -> vn^T and (Z R)^T
-//   E2 o = e^G (q S0) + Z R and vn staged in shared memory, bulk-stored
+//   E2 o = e^G (q S0) + Z R and vn staged in shared memory, then written with
+//      coalesced 16-byte stores
 // The state is read once, at tensor-core rate, and everything else stays on
 // chip.  Every wait is bounded (~1 s); on timeout the CTA raises
 // DFT_DEV_TIMEOUT, drains what it issued (bounded), frees TMEM and exits.
@@ -51,24 +54,25 @@ constexpr uint32_t COL_M0 = 0, COL_M1 = 32, COL_M2 = 160;
 constexpr uint32_t kS0Bytes = 64 * 1024;   // one state tile: 4 K-blocks [128 x 128 B]
 constexpr uint32_t OFF_S0 = 0;
 constexpr uint32_t OFF_KQ = 64 * 1024;     // [k; q] operand (4 K-blocks [64 x 128 B]); then [X; Z] hi, lo of head h at +16 KB h
-constexpr uint32_t OFF_RT = 96 * 1024;     // head h at +32 KB h: R^T hi, lo (16 KB each), then vn | o staging
-                                           // (head 1's region stages k_hat first)
-constexpr uint32_t OFF_U = 160 * 1024;     // head h at +12 KB h: A, PD, X (4 KB each)
-constexpr uint32_t U_A = 0, U_PD = 4096, U_X = 8192, kUHead = 12288;
+constexpr uint32_t OFF_RT = 96 * 1024;     // head 1's state tile (TMA) until its M1 retires; then head h at
+                                           // +32 KB h: R^T hi, lo (16 KB each), then vn | o staging
+constexpr uint32_t OFF_U = 160 * 1024;     // head h at +12 KB h: A, PD, A' (4 KB each; A'[p][q] = A[31-q][31-p])
+constexpr uint32_t U_A = 0, U_PD = 4096, U_AT = 8192, kUHead = 12288;
 constexpr uint32_t OFF_SMALL = 184 * 1024;
 constexpr uint32_t kSmallBytes = 4096;
 constexpr uint32_t OFF_ACT = 188 * 1024;   // (2 + R) parts x (conv rows + 32 node rows) x 128 bf16 channels
 constexpr uint32_t kMaxSmem = 227 * 1024;
 
 struct Small {
-  unsigned long long bar_s, bar_x, bar_m0, bar_m1[2], bar_m2[2], bar_dr;
+  unsigned long long bar_s, bar_s1, bar_x, bar_m0, bar_m1[2], bar_m2[2], bar_dr;
   uint32_t tmem_base;
   int abort;
-  uint32_t anc[kNP];               // bit j: j is i or an ancestor of i
-  uint32_t taps[kNP];              // tile rows of conv taps 0..2 (one byte each; tap 3 is the node)
-  __align__(16) float g[2][kNP];
-  __align__(16) float G[2][kNP];
-  float beta[2][kNP], eG[2][kNP];
+  // per-unit inputs, double-buffered: unit u uses buffer (its ordinal) % 2
+  // while the next unit's are prepared in the other
+  uint32_t anc[2][kNP];            // bit j: j is i or an ancestor of i
+  uint32_t taps[2][kNP];           // tile rows of conv taps 0..2 (one byte each; tap 3 is the node)
+  __align__(16) float G[2][2][kNP];   // [buffer][v-head][node]
+  float beta[2][2][kNP], eG[2][2][kNP];
 };
 static_assert(sizeof(Small) <= kSmallBytes, "small region");
 
@@ -106,12 +110,20 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// L2 policy for data read exactly once (states, activation tiles): evicted
+// first, so that the streamed tiles do not push the kernel's instructions
+// and the small per-request inputs out of L2
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint32_t bar) {
+                                            uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(policy)
       : "memory");
 }
 
@@ -176,20 +188,12 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
-__device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit_and_wait_read() {
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                            uint32_t bar) {
+                                            uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "l"(policy)
       : "memory");
 }
 __device__ __forceinline__ void named_bar(int id, int threads) {
@@ -233,10 +237,24 @@ __device__ __forceinline__ int sq32(int i, int j) { return i * 32 + ((((j >> 2) 
 struct TcArgs {
   dft_gdn_args g;
   dft_gdn_conv_args cv;
-  int vn_rows;     // 1: vn rows are 128 floats apart (one bulk copy per tile)
-  int k_rows;      // 1: k_hat rows are 128 floats apart
 };
 
+// global loads the compiler keeps where they are written (prefetch one unit ahead)
+__device__ __forceinline__ uint4 ldg_keep_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t ldg_keep_u32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ unsigned short ldg_keep_u16(const void* p) {
+  unsigned short r;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+  return r;
+}
 __device__ __forceinline__ uint32_t ld_s32(const unsigned char* p) { return *reinterpret_cast<const uint32_t*>(p); }
 __device__ __forceinline__ void st_s32(unsigned char* p, uint32_t v) { *reinterpret_cast<uint32_t*>(p) = v; }
 
@@ -251,6 +269,65 @@ __device__ __forceinline__ float4 ld4(const unsigned char* p, __nv_bfloat16) {
 __device__ __forceinline__ int part_channel(int p, int hk, int Hk, int R) {
   const int KD = Hk * kD;
   return p == 0 ? hk * kD : (p == 1 ? KD + hk * kD : 2 * KD + (hk * R + p - 2) * kD);
+}
+
+// Per-unit masks and gates of unit u into buffer buf, by warps 13-15 (warp
+// 15: ancestor masks and conv taps; warps 13, 14: gates of v-head warp - 13).
+template <int R, bool CONV>
+__device__ __forceinline__ void prep_unit(const dft_gdn_args& a, const dft_gdn_conv_args& cv, Small& sm,
+                                          int32_t* status, int u, int buf, int warp, int lane) {
+  const int N = a.N, Hk = a.Hk;
+    const int b = u / Hk, hk = u % Hk;
+    {
+      const int n = lane;
+      const uint32_t m = anc_mask_warp(a.anc, b, N, lane);
+      if (warp == 15) {
+        sm.anc[buf][n] = m;
+        if (CONV) {
+          uint32_t packed = 0;
+          if (n < N) {
+            const int64_t* ci = cv.cidx + ((int64_t)b * N + n) * 4;
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+              int64_t c = ci[j];
+              if (c < 0 || c >= 3 + N) {
+                raise_status(status, DFT_DEV_BAD_INDEX);
+                c = 3 + n;
+              }
+              packed |= (uint32_t)c << (8 * j);
+            }
+            if (ci[3] != 3 + n) raise_status(status, DFT_DEV_BAD_INDEX);   // tap 3 is the node itself
+          }
+          sm.taps[buf][n] = packed;
+        }
+      } else if (warp - 13 < R) {
+        // g, beta, G = sum of g over the ancestors in ascending order (tree_kernels.py:146-153)
+        const int hl = warp - 13, h = hk * R + hl;
+        float g = 0.f, beta = 0.f;
+        if (n < N) {
+          // raw loads first, conversions after (one memory round trip)
+          const int64_t ab = (int64_t)b * a.ab_sb + (int64_t)n * a.ab_sn + h;
+          const uint32_t ra = ld_bits(a.a, a.ab_dtype, ab), rb = ld_bits(a.bg, a.ab_dtype, ab);
+          const uint32_t rd = ld_bits(a.dt_bias, a.dtb_dtype, h);
+          const float dec = a.neg_exp_A ? __ldg(a.neg_exp_A + h) : -expf(__ldg(a.A_log + h));
+          const float ar = bits_f32(ra, a.ab_dtype) + bits_f32(rd, a.dtb_dtype);
+          const float sp = ar > 20.f ? ar : logf(1.f + expf(fminf(ar, 20.f)));
+          g = dec * sp;
+          beta = 1.f / (1.f + expf(-bits_f32(rb, a.ab_dtype)));
+        }
+        float G = 0.f;
+#pragma unroll 1
+        for (int j = 0; j < kNP; ++j) {
+          const float gj = __shfl_sync(0xffffffffu, g, j);
+          if ((m >> j) & 1u) G += gj;
+        }
+        sm.G[buf][hl][n] = G;
+        sm.beta[buf][hl][n] = beta;
+        sm.eG[buf][hl][n] = expf(G);
+        if (a.aux_g && n < N) a.aux_g[(int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh + n] = G;
+      }
+      __syncwarp();
+    }
 }
 
 template <int R, bool CONV>
@@ -273,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kRowB = kD * 2;                        // bytes per tile row
   constexpr int kPartB = (kOff + kNP) * kRowB;         // bytes per activation part
   constexpr uint32_t kBox = kNP * kRowB;               // one TMA box: 32 node rows
-  const uint32_t bar_s = smem_u32(&sm.bar_s), bar_x = smem_u32(&sm.bar_x);
+  const uint32_t bar_s = smem_u32(&sm.bar_s), bar_s1 = smem_u32(&sm.bar_s1), bar_x = smem_u32(&sm.bar_x);
   const uint32_t bar_m0 = smem_u32(&sm.bar_m0), bar_dr = smem_u32(&sm.bar_dr);
   const uint32_t bar_m1[2] = {smem_u32(&sm.bar_m1[0]), smem_u32(&sm.bar_m1[1])};
   const uint32_t bar_m2[2] = {smem_u32(&sm.bar_m2[0]), smem_u32(&sm.bar_m2[1])};
@@ -286,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (ctl_warp) {
     if (lane == 0) {
       mbar_init(bar_s, 1);
+      mbar_init(bar_s1, 1);
       mbar_init(bar_x, 1);
       mbar_init(bar_m0, 1);
       mbar_init(bar_m1[0], 1);
@@ -309,15 +387,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  // state of v-head hl of unit u into the slot
+  const uint64_t once = l2_evict_first();
+  // state of v-head hl of unit u: head 0 into the state slot, head 1 into the
+  // R^T region (free from the end of the previous unit until this unit's M1
+  // of head 1 has retired)
   auto issue_state = [&](int u, int hl) {
     const int b = u / Hk, hk = u % Hk;
     const long long s = a.state_slots ? a.state_slots[b] : b;
     const int slot = s < 0 ? 0 : (int)s;
-    mbar_expect_tx(bar_s, kS0Bytes);
+    const uint32_t bar = hl ? bar_s1 : bar_s, dst = sbase + (hl ? OFF_RT : OFF_S0);
+    mbar_expect_tx(bar, kS0Bytes);
 #pragma unroll
-    for (int kb = 0; kb < 4; ++kb)
-      tma_load_4d(sbase + OFF_S0 + kb * 16384, &pool_map, 32 * kb, 0, hk * R + hl, slot, bar_s);
+    for (int kb = 0; kb < 4; ++kb) tma_load_4d(dst + kb * 16384, &pool_map, 32 * kb, 0, hk * R + hl, slot, bar, once);
   };
   // the unit's activation tile: q, k and R v column blocks x 32 node rows
   auto issue_act = [&](int u) {
@@ -325,16 +406,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_expect_tx(bar_x, (2 + R) * kBox);
 #pragma unroll
     for (int p = 0; p < 2 + R; ++p)
-      tma_load_3d(sbase + OFF_ACT + p * kPartB + kOff * kRowB, &act_map, part_channel(p, hk, Hk, R), 0, b, bar_x);
+      tma_load_3d(sbase + OFF_ACT + p * kPartB + kOff * kRowB, &act_map, part_channel(p, hk, Hk, R), 0, b, bar_x,
+                  once);
   };
   // control-thread bookkeeping for the drain on timeout
-  int s_issued = 0, s_used = 0, x_issued = 0, x_used = 0;
+  int s_issued = 0, s_used = 0, s1_issued = 0, s1_used = 0, x_issued = 0, x_used = 0;
   if (ctl_warp) {
     if (lane == 0 && (int)blockIdx.x < units) {
-      issue_state(blockIdx.x, 0);
       issue_act(blockIdx.x);
+      issue_state(blockIdx.x, 0);
       s_issued = 1;
       x_issued = 1;
+      if (R == 2) {
+        issue_state(blockIdx.x, 1);
+        s1_issued = 1;
+      }
     }
     __syncwarp();   // the control warp reconverges before the next CTA barrier
   }
@@ -351,75 +437,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const dft_gdn_conv_args& cv = ta.cv;
     const int b = u / Hk, hk = u % Hk;
     const int col = part_channel(cpart, hk, Hk, R) + cpair;
-    // bf16 weights [C][4]: channels col, col + 1 are 16 contiguous bytes
-    pw = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(cv.weight) + (int64_t)col * 4));
-    pb = cv.bias ? __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(cv.bias) + col)) : 0u;
+    // bf16 weights [C][4]: channels col, col + 1 are 16 contiguous bytes.  The
+    // loads are volatile so that they issue here, a unit ahead of their use,
+    // rather than being re-issued next to it
+    pw = ldg_keep_v4(reinterpret_cast<const uint16_t*>(cv.weight) + (int64_t)col * 4);
+    pb = cv.bias ? ldg_keep_u32(reinterpret_cast<const uint16_t*>(cv.bias) + col) : 0u;
     const long long cslot = cv.conv_slots ? cv.conv_slots[b] : b;
     const uint16_t* cs = reinterpret_cast<const uint16_t*>(cv.conv_state);
     const int64_t c0 = cslot * cv.cs_ss + (int64_t)col * cv.cs_sc, c1 = c0 + cv.cs_sc;
     // raw loads only: nothing here waits for them (they are consumed a unit later)
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-      ps[2 * j] = __ldg(cs + c0 + j * cv.cs_st);
-      ps[2 * j + 1] = __ldg(cs + c1 + j * cv.cs_st);
+      ps[2 * j] = ldg_keep_u16(cs + c0 + j * cv.cs_st);
+      ps[2 * j + 1] = ldg_keep_u16(cs + c1 + j * cv.cs_st);
     }
   };
   if (conv_thr && (int)blockIdx.x < units) load_conv(blockIdx.x);
+  if (warp >= 13 && (int)blockIdx.x < units) prep_unit<R, CONV>(a, ta.cv, sm, status, blockIdx.x, 0, warp, lane);
 
   int it = 0;
   for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
     const int b = u / Hk, hk = u % Hk;
     const uint32_t ph = it & 1;
-    // ------------------------------------------------ F0: masks and gates (before the tile lands)
-    if (warp >= 13) {
-      // warp 15: ancestor masks and conv taps; warps 13, 14: gates of v-head warp - 13
-      const int n = lane;
-      const uint32_t m = anc_mask_warp(a.anc, b, N, lane);
-      if (warp == 15) {
-        sm.anc[n] = m;
-        if (CONV) {
-          uint32_t packed = 0;
-          if (n < N) {
-            const int64_t* ci = ta.cv.cidx + ((int64_t)b * N + n) * 4;
-#pragma unroll
-            for (int j = 0; j < 3; ++j) {
-              int64_t c = ci[j];
-              if (c < 0 || c >= 3 + N) {
-                raise_status(status, DFT_DEV_BAD_INDEX);
-                c = 3 + n;
-              }
-              packed |= (uint32_t)c << (8 * j);
-            }
-            if (ci[3] != 3 + n) raise_status(status, DFT_DEV_BAD_INDEX);   // tap 3 is the node itself
-          }
-          sm.taps[n] = packed;
-        }
-      } else if (warp - 13 < R) {
-        // g, beta, G = sum of g over the ancestors in ascending order (tree_kernels.py:146-153)
-        const int hl = warp - 13, h = hk * R + hl;
-        float g = 0.f, beta = 0.f;
-        if (n < N) {
-          // raw loads first, conversions after (one memory round trip)
-          const int64_t ab = (int64_t)b * a.ab_sb + (int64_t)n * a.ab_sn + h;
-          const uint32_t ra = ld_bits(a.a, a.ab_dtype, ab), rb = ld_bits(a.bg, a.ab_dtype, ab);
-          const uint32_t rd = ld_bits(a.dt_bias, a.dtb_dtype, h);
-          const float dec = a.neg_exp_A ? __ldg(a.neg_exp_A + h) : -expf(__ldg(a.A_log + h));
-          const float ar = bits_f32(ra, a.ab_dtype) + bits_f32(rd, a.dtb_dtype);
-          const float sp = ar > 20.f ? ar : logf(1.f + expf(fminf(ar, 20.f)));
-          g = dec * sp;
-          beta = 1.f / (1.f + expf(-bits_f32(rb, a.ab_dtype)));
-        }
-        sm.g[hl][n] = g;
-        __syncwarp();
-        float G = 0.f;
-        for (uint32_t mm = m; mm; mm &= mm - 1) G += sm.g[hl][__ffs(mm) - 1];
-        sm.G[hl][n] = G;
-        sm.beta[hl][n] = beta;
-        sm.eG[hl][n] = expf(G);
-        if (a.aux_g && n < N) a.aux_g[(int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh + n] = G;
-      }
-      __syncwarp();
-    }
+    const int cb = it & 1;   // this unit's buffer of per-unit inputs
     // ------------------------------------------------ F1: the activation tile
     if (!mbar_wait(bar_x, ph)) atomicExch(&sm.abort, 1);
     if (ctl) ++x_used;
@@ -459,23 +499,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (; n >= 3; n -= 4) {
         // all four nodes read their taps before any writes (a lower one may be a tap)
-        const f32x2 ya = node(sm.taps[n], n);
-        const f32x2 yb = node(sm.taps[n - 1], n - 1);
-        const f32x2 yc = node(sm.taps[n - 2], n - 2);
-        const f32x2 yd = node(sm.taps[n - 3], n - 3);
+        const f32x2 ya = node(sm.taps[cb][n], n);
+        const f32x2 yb = node(sm.taps[cb][n - 1], n - 1);
+        const f32x2 yc = node(sm.taps[cb][n - 2], n - 2);
+        const f32x2 yd = node(sm.taps[cb][n - 3], n - 3);
         st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(ya));
         st_s32(colp + (2 + n) * kRowB, f32x2_to_bf16x2(yb));
         st_s32(colp + (1 + n) * kRowB, f32x2_to_bf16x2(yc));
         st_s32(colp + n * kRowB, f32x2_to_bf16x2(yd));
       }
 #pragma unroll 1
-      for (; n >= 0; --n) st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(node(sm.taps[n], n)));
+      for (; n >= 0; --n) st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(node(sm.taps[cb][n], n)));
     }
-    if (CONV) __syncthreads();
+    if (warp >= 13) {
+      const int nu = u + gridDim.x;
+      if (nu < units) prep_unit<R, CONV>(a, ta.cv, sm, status, nu, cb ^ 1, warp, lane);
+    }
+    __syncthreads();
     // ------------------------------------------------ F3: norms, [k; q] operand, k_hat rows
     {
       // warp w: nodes w and w + 16, q and k, as four independent chains
-      float* kst = reinterpret_cast<float*>(smem + OFF_RT + 32768);   // k_hat staging [n][128] fp32
       const int kb = lane >> 3, ch = lane & 7;                         // K-block, 16-byte chunk of channels 4 lane..
       float4 v[2][2];
       float ss[2][2];
@@ -512,8 +555,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               y.y *= a.scale;
               y.z *= a.scale;
               y.w *= a.scale;
-            } else {
-              *reinterpret_cast<float4*>(kst + n * kD + lane * 4) = y;
+            } else if (a.aux_k) {
+              // k_hat row n -> aux_k: 16 bytes per lane, one coalesced 512-byte row per warp
+              const int heads = a.aux_k_per_v ? R : 1;
+              for (int hh = 0; hh < heads; ++hh) {
+                float* g = a.aux_k + (int64_t)b * a.ak_sb + (int64_t)(a.aux_k_per_v ? hk * R + hh : hk) * a.ak_sh +
+                           (int64_t)n * a.ak_sn + lane * 4;
+                *reinterpret_cast<float4*>(g) = y;
+              }
             }
           }
           const int row = p == 0 ? 32 + n : n;   // k rows 0..31, q rows 32..63
@@ -549,28 +598,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bar_m1[0]);
         if (R == 2) {
-          // head 1's state into the slot once head 0's M1 has read it
-          if (!mbar_wait(bar_m1[0], ph)) atomicExch(&sm.abort, 1);
-          issue_state(u, 1);
-          ++s_issued;
+          if (!mbar_wait(bar_s1, s1_used & 1)) atomicExch(&sm.abort, 1);
+          ++s1_used;
+          tc_fence_after();
+  #pragma unroll 1
+          for (int kb = 0; kb < 4; ++kb) {
+            const uint64_t da = sw128_desc(sbase + OFF_RT + kb * 16384);
+            const uint64_t db = sw128_desc(sbase + OFF_KQ + kb * 8192);
+  #pragma unroll
+            for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1 + 64, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
+          }
+          mma_commit(bar_m1[1]);
         }
       }
       __syncwarp();   // the control warp reconverges before the next CTA barrier
-    }
-    // k_hat rows -> aux_k (one warp; the staging is free again before head 1's E1)
-    if (warp == 8 && a.aux_k) {
-      const int heads = a.aux_k_per_v ? R : 1;
-      const float* kst = reinterpret_cast<const float*>(smem + OFF_RT + 32768);
-      for (int hh = 0; hh < heads; ++hh) {
-        float* g = a.aux_k + (int64_t)b * a.ak_sb + (int64_t)(a.aux_k_per_v ? hk * R + hh : hk) * a.ak_sh;
-        if (ta.k_rows) {
-          if (lane == 0) bulk_store(g, smem_u32(kst), N * kD * 4);
-        } else if (lane < N) {
-          bulk_store(g + (int64_t)lane * a.ak_sn, smem_u32(kst + lane * kD), kD * 4);
-        }
-      }
-      bulk_commit_and_wait_read();
-      __syncwarp();
     }
     // ------------------------------------------------ C1: A and PD of every head (8 warps)
     // warp w: rows from TMEM lanes 32 (w % 4) (k.k^T for w % 4 == 0, q.k^T for 1),
@@ -584,103 +625,104 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + COL_M0 + 16 * half, kk);
       // A: strict ancestors, beta_i k.k^T e^{G_i-G_j}; PD: ancestors, q.k^T e^{G_i-G_j}
       const int i = lane;
-      const uint32_t keep = pd ? sm.anc[i] : sm.anc[i] & ~(1u << i);
-      const float Gi = sm.G[hh][i], ci = pd ? 1.f : sm.beta[hh][i];
+      const uint32_t keep = pd ? sm.anc[cb][i] : sm.anc[cb][i] & ~(1u << i);
+      const float Gi = sm.G[cb][hh][i], ci = pd ? 1.f : sm.beta[cb][hh][i];
       float* dst = reinterpret_cast<float*>(smem + OFF_U + hh * kUHead + (pd ? U_PD : U_A));
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int j0 = 16 * half + 4 * c;
-        const float4 gj = *reinterpret_cast<const float4*>(&sm.G[hh][j0]);
+        const float4 gj = *reinterpret_cast<const float4*>(&sm.G[cb][hh][j0]);
         float4 o;
         o.x = ((keep >> j0) & 1u) ? ci * kk[4 * c] * __expf(Gi - gj.x) : 0.f;
         o.y = ((keep >> (j0 + 1)) & 1u) ? ci * kk[4 * c + 1] * __expf(Gi - gj.y) : 0.f;
         o.z = ((keep >> (j0 + 2)) & 1u) ? ci * kk[4 * c + 2] * __expf(Gi - gj.z) : 0.f;
         o.w = ((keep >> (j0 + 3)) & 1u) ? ci * kk[4 * c + 3] * __expf(Gi - gj.w) : 0.f;
         *reinterpret_cast<float4*>(dst + sq32(i, j0)) = o;
+        if (!pd) {
+          // A'[31 - j][31 - i] = A[i][j]: lane i writes column 31 - i of four rows
+          float* at = reinterpret_cast<float*>(smem + OFF_U + hh * kUHead + U_AT);
+          at[sq32(31 - j0, 31 - i)] = o.x;
+          at[sq32(30 - j0, 31 - i)] = o.y;
+          at[sq32(29 - j0, 31 - i)] = o.z;
+          at[sq32(28 - j0, 31 - i)] = o.w;
+        }
       }
     }
     __syncthreads();
     if (sm.abort) break;
-    // ------------------------------------------------ X = (I + A)^-1 per head (warps 2, 6); head 1's M1
-    if ((warp & 3) == 2 && (warp >> 2) < R) {
-      // one column per lane, kept in registers
-      const float* A = reinterpret_cast<const float*>(smem + OFF_U + (warp >> 2) * kUHead + U_A);
-      float* X = reinterpret_cast<float*>(smem + OFF_U + (warp >> 2) * kUHead + U_X);
-      const int c = lane;
-      float xc[32];
+    // ------------------------------------------------ X, Z per head (warps 2, 3 / 6, 7)
+    // Both are unit lower-triangular solves r_i = init_i - sum_{m < i} L[i][m] r_m,
+    // one column / row per lane, in registers:
+    //   X = (I + A)^-1:  L = A,  init = e_c (lane c = column c of X)
+    //   Z = PD X, i.e. Z (I + A) = PD:  L = A' (A'[p][q] = A[31-q][31-p]),
+    //   init = row n of PD reversed, z_j = r_{31-j} (lane n = row n of Z)
+    // They go into the [X; Z] operand (hi / lo tf32 split) over [k; q] once
+    // every M1 has retired.
+    if ((warp & 3) >= 2 && (warp >> 2) < R) {
+      const int hh = warp >> 2;
+      const bool zw = warp & 1;
+      const float* L = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + (zw ? U_AT : U_A));
+      float r[32];
+      if (!zw) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 32; ++i) r[i] = i == lane ? 1.f : 0.f;
+      } else {
+        const float* PD = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + U_PD);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 q = *reinterpret_cast<const float4*>(PD + sq32(lane, 4 * c));
+          r[31 - 4 * c] = q.x;
+          r[30 - 4 * c] = q.y;
+          r[29 - 4 * c] = q.z;
+          r[28 - 4 * c] = q.w;
+        }
+      }
+#pragma unroll
+      for (int i = 1; i < 32; ++i) {
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
         for (int m = 0; m < i; m += 4) {
-          s0 = fmaf(A[sq32(i, m)], xc[m], s0);
-          if (m + 1 < i) s1 = fmaf(A[sq32(i, m + 1)], xc[m + 1], s1);
-          if (m + 2 < i) s2 = fmaf(A[sq32(i, m + 2)], xc[m + 2], s2);
-          if (m + 3 < i) s3 = fmaf(A[sq32(i, m + 3)], xc[m + 3], s3);
+          s0 = fmaf(L[sq32(i, m)], r[m], s0);
+          if (m + 1 < i) s1 = fmaf(L[sq32(i, m + 1)], r[m + 1], s1);
+          if (m + 2 < i) s2 = fmaf(L[sq32(i, m + 2)], r[m + 2], s2);
+          if (m + 3 < i) s3 = fmaf(L[sq32(i, m + 3)], r[m + 3], s3);
         }
-        xc[i] = (i == c ? 1.f : 0.f) - ((s0 + s1) + (s2 + s3));
-        X[i * 32 + c] = xc[i];
+        r[i] = r[i] - ((s0 + s1) + (s2 + s3));
       }
-    }
-    if (ctl_warp) {
-      if (R == 2 && lane == 0) {
-        if (!mbar_wait(bar_s, s_used & 1)) atomicExch(&sm.abort, 1);
-        ++s_used;
-        tc_fence_after();
-        const uint32_t id1 = idesc_tf32(128, 64);
-  #pragma unroll 1
-        for (int kb = 0; kb < 4; ++kb) {
-          const uint64_t da = sw128_desc(sbase + OFF_S0 + kb * 16384);
-          const uint64_t db = sw128_desc(sbase + OFF_KQ + kb * 8192);
-  #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1 + 64, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
-        }
-        mma_commit(bar_m1[1]);
-      }
-      __syncwarp();   // the control warp reconverges before the next CTA barrier
-    }
-    __syncthreads();
-    if (sm.abort) break;
-    // ------------------------------------------------ [X; Z] operands (warps 0-7) and E1 (warps 8-15)
-    if (tid < 256) {
-      // rows 0..31 X, rows 32..63 Z = PD X, hi / lo tf32 split, over [k; q] once every M1 has retired
-      if (!mbar_wait(bar_m1[R - 1], ph)) atomicExch(&sm.abort, 1);
-      const int n = tid >> 3, c = tid & 7;   // row n, 16-byte chunk c (columns 4c..4c+3)
-#pragma unroll 1
-      for (int hh = 0; hh < R; ++hh) {
-        const float* PD = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + U_PD);
-        const float* X = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + U_X);
-        unsigned char* xzh = smem + OFF_KQ + hh * 16384;
-        unsigned char* xzl = xzh + 8192;
-        float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-        for (int j = 0; j < 32; ++j) {
-          const float pdv = PD[sq32(n, j)];
-          const float4 xr = *reinterpret_cast<const float4*>(X + j * 32 + 4 * c);
-          z.x = fmaf(pdv, xr.x, z.x);
-          z.y = fmaf(pdv, xr.y, z.y);
-          z.z = fmaf(pdv, xr.z, z.z);
-          z.w = fmaf(pdv, xr.w, z.w);
-        }
-        const float4 xv = *reinterpret_cast<const float4*>(X + n * 32 + 4 * c);
+      if (!mbar_wait(bar_m1[R - 1], ph)) atomicExch(&sm.abort, 1);   // [k; q] is free
+      unsigned char* xzh = smem + OFF_KQ + hh * 16384;
+      unsigned char* xzl = xzh + 8192;
+      if (!zw) {
+        // lane c writes column c of every X row i (a full 128-byte row per step)
+        const int c = lane;
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const float4 v = q ? z : xv;
-          const int row = q ? 32 + n : n;
+        for (int i = 0; i < 32; ++i) {
+          const uint32_t off = (uint32_t)(i * 128 + ((((c >> 2) ^ i) & 7) << 4) + (c & 3) * 4);
+          const float hi = tf32_rna(r[i]);
+          *reinterpret_cast<float*>(xzh + off) = hi;
+          *reinterpret_cast<float*>(xzl + off) = tf32_rna(r[i] - hi);
+        }
+      } else {
+        // lane n writes Z row n (z_j = r_{31-j}) as operand row 32 + n
+        const int row = 32 + lane;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
           float4 hi, lo;
-          hi.x = tf32_rna(v.x); lo.x = tf32_rna(v.x - hi.x);
-          hi.y = tf32_rna(v.y); lo.y = tf32_rna(v.y - hi.y);
-          hi.z = tf32_rna(v.z); lo.z = tf32_rna(v.z - hi.z);
-          hi.w = tf32_rna(v.w); lo.w = tf32_rna(v.w - hi.w);
+          hi.x = tf32_rna(r[31 - 4 * c]); lo.x = tf32_rna(r[31 - 4 * c] - hi.x);
+          hi.y = tf32_rna(r[30 - 4 * c]); lo.y = tf32_rna(r[30 - 4 * c] - hi.y);
+          hi.z = tf32_rna(r[29 - 4 * c]); lo.z = tf32_rna(r[29 - 4 * c] - hi.z);
+          hi.w = tf32_rna(r[28 - 4 * c]); lo.w = tf32_rna(r[28 - 4 * c] - hi.w);
           const uint32_t off = (uint32_t)(row * 128 + ((c ^ (row & 7)) << 4));
           *reinterpret_cast<float4*>(xzh + off) = hi;
           *reinterpret_cast<float4*>(xzl + off) = lo;
         }
       }
-    } else if (((warp - 8) >> 2) < R) {
+    }
+    // ------------------------------------------------ E1 (warps 8-15), alongside the X / Z solves
+    if (warp >= 8 && ((warp - 8) >> 2) < R) {
       // E1: R = beta (v - e^G (k S0)) by the four warps owning head hh's TMEM lanes
       const int hh = (warp - 8) >> 2;
-      if (!mbar_wait(bar_m1[hh], ph)) atomicExch(&sm.abort, 1);
+      if (!mbar_wait(bar_m1[R - 1], ph)) atomicExch(&sm.abort, 1);   // R^T region free, (k S0) ready
       tc_fence_after();
       float ks_[kNP];
       tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + COL_M1 + 64 * hh, ks_);
@@ -697,7 +739,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int n = 4 * c + e;
-          const float rr = sm.beta[hh][n] * (to_f32(yv[n * kD]) - sm.eG[hh][n] * ks_[n]);
+          const float rr = sm.beta[cb][hh][n] * (to_f32(yv[n * kD]) - sm.eG[cb][hh][n] * ks_[n]);
           phi[e] = tf32_rna(rr);
           plo[e] = tf32_rna(rr - phi[e]);
         }
@@ -716,8 +758,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // every M1 of this unit has retired and the tile is consumed: request the next unit's
         const int nu = u + gridDim.x;
         if (nu < units) {
-          issue_state(nu, 0);
-          issue_act(nu);
+          issue_act(nu);        // needed first (the next unit's conv)
+          issue_state(nu, 0);   // needed at its M1
           ++s_issued;
           ++x_issued;
         }
@@ -739,55 +781,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();   // the control warp reconverges before the next CTA barrier
     }
-    // ------------------------------------------------ E2: vn and o = e^G (q S0) + Z R, bulk-stored
+    // ------------------------------------------------ E2: vn and o = e^G (q S0) + Z R
+    // thread v stages column v of vn / o over R^T (read by M2); then each of the
+    // head's four warps stores eight rows with coalesced 16-byte stores
     if (warp >= 8 && ((warp - 8) >> 2) < R) {
       const int hh = (warp - 8) >> 2;
       if (!mbar_wait(bar_m2[hh], ph)) atomicExch(&sm.abort, 1);
       tc_fence_after();
       const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
       const int h = hk * R + hh, v = tid & 127;
-      float* vst = reinterpret_cast<float*>(smem + OFF_RT + hh * 32768);            // [n][128] f32, over R^T
+      float* vst = reinterpret_cast<float*>(smem + OFF_RT + hh * 32768);            // [n][128] f32
       T* ost = reinterpret_cast<T*>(smem + OFF_RT + hh * 32768 + 16384);            // [n][128] bf16
-      {
-        float vn[32];
-        tmem_ld32(tmem + lanes + COL_M2 + 64 * hh, vn);
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        float vn[16], zr[16], qs[16];
+        tmem_ld16(tmem + lanes + COL_M2 + 64 * hh + 16 * half, vn);
+        tmem_ld16(tmem + lanes + COL_M2 + 64 * hh + 32 + 16 * half, zr);
+        tmem_ld16(tmem + lanes + COL_M1 + 64 * hh + 32 + 16 * half, qs);
 #pragma unroll
-        for (int n = 0; n < kNP; ++n) vst[n * kD + v] = vn[n];
+        for (int e = 0; e < 16; ++e) {
+          const int n = 16 * half + e;
+          vst[n * kD + v] = vn[e];
+          ost[n * kD + v] = __float2bfloat16_rn(sm.eG[cb][hh][n] * qs[e] + zr[e]);
+        }
       }
-      {
-        float zr[32], qs[32];
-        tmem_ld32(tmem + lanes + COL_M2 + 64 * hh + 32, zr);
-        tmem_ld32(tmem + lanes + COL_M1 + 64 * hh + 32, qs);
-#pragma unroll
-        for (int n = 0; n < kNP; ++n) ost[n * kD + v] = __float2bfloat16_rn(sm.eG[hh][n] * qs[n] + zr[n]);
-      }
-      fence_async_smem();
       named_bar(1 + hh, 128);
-      if ((warp & 3) == 0) {
-        const int n = lane;
-        if (a.aux_vn) {
-          float* g = a.aux_vn + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh;
-          if (ta.vn_rows) {
-            if (n == 0) bulk_store(g, smem_u32(vst), N * kD * 4);
-          } else if (n < N) {
-            bulk_store(g + (int64_t)n * a.av_sn, smem_u32(vst + n * kD), kD * 4);
-          }
+      const int r0 = 8 * (warp & 3);
+      if (a.aux_vn) {
+        float* g = a.aux_vn + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh + lane * 4;
+#pragma unroll 4
+        for (int e = 0; e < 8; ++e) {
+          const int n = r0 + e;
+          if (n < N)
+            *reinterpret_cast<float4*>(g + (int64_t)n * a.av_sn) = *reinterpret_cast<const float4*>(vst + n * kD + lane * 4);
         }
-        if (n < N) {
-          T* g = reinterpret_cast<T*>(a.o) + (int64_t)b * a.o_sb + (int64_t)n * a.o_sn + (int64_t)h * a.o_sh;
-          bulk_store(g, smem_u32(ost + n * kD), kD * 2);
+      }
+      {
+        T* g = reinterpret_cast<T*>(a.o) + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + (lane & 15) * 8;
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const int n = r0 + e + (lane >> 4);   // lanes 0-15 one row, 16-31 the next
+          if (n < N)
+            *reinterpret_cast<uint4*>(g + (int64_t)n * a.o_sn) = *reinterpret_cast<const uint4*>(ost + n * kD + (lane & 15) * 8);
         }
-        bulk_commit_and_wait_read();
-        __syncwarp();
       }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (sm.abort) break;
+    if (ctl_warp) {
+      if (R == 2 && lane == 0) {
+        // the staging in the R^T region has been read: the next unit's head-1 state goes there
+        const int nu = u + gridDim.x;
+        if (nu < units) {
+          issue_state(nu, 1);
+          ++s1_issued;
+        }
+      }
+      __syncwarp();   // the control warp reconverges before the next CTA barrier
+    }
   }
   // ------------------------------------------------ teardown
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // own output copies complete
   __syncthreads();
   if (sm.abort) {
     if (ctl_warp) {
@@ -795,6 +850,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         raise_status(status, DFT_DEV_TIMEOUT);
         // drain what this CTA issued before freeing its shared memory / TMEM (bounded)
         for (; s_used < s_issued; ++s_used) mbar_wait(bar_s, s_used & 1);
+        for (; s1_used < s1_issued; ++s1_used) mbar_wait(bar_s1, s1_used & 1);
         for (; x_used < x_issued; ++x_used) mbar_wait(bar_x, x_used & 1);
         mma_commit(bar_dr);   // arrives once every MMA this thread issued has retired
         mbar_wait(bar_dr, 0);
@@ -911,8 +967,6 @@ int dft_gdn_tc_launch(const dft_gdn_args* a, int32_t* status, cudaStream_t st) {
   ta.g = *a;
   if (a->conv) ta.cv = *a->conv;
   else memset(&ta.cv, 0, sizeof(ta.cv));
-  ta.vn_rows = a->av_sn == kD;
-  ta.k_rows = a->ak_sn == kD;
   const int R = a->Hv / a->Hk;
   const bool conv = a->conv != nullptr;
   const uint32_t smem = smem_bytes(R, conv);

@@ -56,7 +56,7 @@ def _layer_inputs(B, N, Hk, Hv, D, seed, dtype, chain_p=0.5):
                 A_log=A_log, dtb=dtb)
 
 
-def _verify(d, Hk, Hv, y=None, conv=False, force_simt=False):
+def _verify(d, Hk, Hv, y=None, conv=False, force_simt=False, status=None):
     from dforktree_b200 import kernels as K
     B, N = d["a"].shape[:2]
     ak = torch.zeros(B, Hk, N, 128, device=DEV)
@@ -64,7 +64,7 @@ def _verify(d, Hk, Hv, y=None, conv=False, force_simt=False):
     ag = torch.zeros(B, Hv, N, device=DEV)
     cv = dict(x=d["x"], conv_state=d["conv_state"], weight=d["weight"], cidx=d["cidx"]) if conv else None
     o = K.gdn_tree_verify(y, d["a"], d["b"], d["A_log"], d["dtb"], d["anc"], d["pool"], Hk, Hv, aux_k=ak,
-                          aux_vn=av, aux_g=ag, aux_k_per_v=False, conv=cv, force_simt=force_simt,
+                          aux_vn=av, aux_g=ag, aux_k_per_v=False, conv=cv, force_simt=force_simt, status=status,
                           o=torch.empty(B, N, Hv, 128, dtype=d["x"].dtype, device=DEV))
     return o, ak, av, ag
 
@@ -75,8 +75,11 @@ def test_fused_conv_verify_equals_separate_conv_then_verify(dtype):
     Hk, Hv = 16, 32
     d = _layer_inputs(4, 32, Hk, Hv, 128, seed=31, dtype=dtype)
     y = K.tree_conv(d["x"], d["conv_state"], d["weight"], None, d["cidx"])
-    ref = _verify(d, Hk, Hv, y=y)
-    got = _verify(d, Hk, Hv, conv=True)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ref = _verify(d, Hk, Hv, y=y, status=st)
+    got = _verify(d, Hk, Hv, conv=True, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
     for r, g_ in zip(ref, got):
         assert torch.equal(r, g_)
 
@@ -88,8 +91,11 @@ def test_tensor_core_verify_matches_simt_and_oracle(dtype, tol, N):
     Hk, Hv, D = 16, 32, 128
     d = _layer_inputs(3, N, Hk, Hv, D, seed=40 + N, dtype=dtype)
     y = K.tree_conv(d["x"], d["conv_state"], d["weight"], None, d["cidx"])
-    tc = _verify(d, Hk, Hv, y=y)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    tc = _verify(d, Hk, Hv, y=y, status=st)
     si = _verify(d, Hk, Hv, y=y, force_simt=True)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
     assert _rel(_np(tc[0]), _np(si[0])) < tol
     assert _rel(_np(tc[2]), _np(si[2])) < 1e-3
     assert _rel(_np(tc[1]), _np(si[1])) < 1e-5
@@ -100,6 +106,25 @@ def test_tensor_core_verify_matches_simt_and_oracle(dtype, tol, N):
         assert _rel(_np(tc[0][r]), oo) < tol, r
         assert _rel(_np(tc[2][r]), ovn) < 1e-3, r
         np.testing.assert_allclose(_np(tc[3][r]), oG, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("N", [32, 17])
+def test_tensor_core_verify_many_units_per_cta(N):
+    """B = 20 requests x 16 k-heads = 320 work units, so every persistent CTA
+    loops over two or three units (state / tile prefetch across units)."""
+    from dforktree_b200 import kernels as K
+    Hk, Hv = 16, 32
+    d = _layer_inputs(20, N, Hk, Hv, 128, seed=90 + N, dtype=torch.bfloat16)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    tc = _verify(d, Hk, Hv, conv=True, status=st)
+    y = K.tree_conv(d["x"], d["conv_state"], d["weight"], None, d["cidx"])
+    si = _verify(d, Hk, Hv, y=y, force_simt=True)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert _rel(_np(tc[0]), _np(si[0])) < 2e-2
+    assert _rel(_np(tc[2]), _np(si[2])) < 1e-3
+    assert _rel(_np(tc[1]), _np(si[1])) < 1e-5
+    np.testing.assert_allclose(_np(tc[3]), _np(si[3]), rtol=1e-5, atol=1e-5)
 
 
 def test_cycle_step_matches_oracle_chain():
