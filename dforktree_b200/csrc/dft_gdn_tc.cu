@@ -26,8 +26,8 @@
 //   E1 R = beta (v - e^G (k S0)) by the thread owning TMEM lane v -> R^T tile
 //      (alongside C's solves)
 //   M2 tcgen05 MMA  D2_h = R^T [X; Z]^T (3xTF32) -> vn^T and (Z R)^T
-//   E2 o = e^G (q S0) + Z R and vn staged in shared memory, then written with
-//      coalesced 16-byte stores
+//   E2 o = e^G (q S0) + Z R and vn from TMEM straight to global memory (per
+//      node row, one warp writes 32 consecutive elements)
 // The state is read once, at tensor-core rate, and everything else stays on
 // chip.  Every wait is bounded (~1 s); on timeout the CTA raises
 // DFT_DEV_TIMEOUT, drains what it issued (bounded), frees TMEM and exits.
@@ -55,7 +55,7 @@ constexpr uint32_t kS0Bytes = 64 * 1024;   // one state tile: 4 K-blocks [128 x 
 constexpr uint32_t OFF_S0 = 0;
 constexpr uint32_t OFF_KQ = 64 * 1024;     // [k; q] operand (4 K-blocks [64 x 128 B]); then [X; Z] hi, lo of head h at +16 KB h
 constexpr uint32_t OFF_RT = 96 * 1024;     // head 1's state tile (TMA) until its M1 retires; then head h at
-                                           // +32 KB h: R^T hi, lo (16 KB each), then vn | o staging
+                                           // +32 KB h: R^T hi, lo (16 KB each) until M2 retires
 constexpr uint32_t OFF_U = 160 * 1024;     // head h at +12 KB h: A, PD, A' (4 KB each; A'[p][q] = A[31-q][31-p])
 constexpr uint32_t U_A = 0, U_PD = 4096, U_AT = 8192, kUHead = 12288;
 constexpr uint32_t OFF_SMALL = 184 * 1024;
@@ -216,13 +216,17 @@ __device__ __forceinline__ float bits_f32(uint32_t v, int dtype) {
 __device__ __forceinline__ uint32_t anc_mask_warp(const float* anc, int b, int N, int lane) {
   uint32_t mine = 0;
   const float* base = anc + (int64_t)b * N * N;
-  float v[kNP];
+  // eight rows in flight per step
+#pragma unroll 1
+  for (int n0 = 0; n0 < kNP; n0 += 8) {
+    float v[8];
 #pragma unroll
-  for (int n = 0; n < kNP; ++n) v[n] = (n < N && lane < N) ? __ldg(base + (int64_t)n * N + lane) : 0.f;
+    for (int e = 0; e < 8; ++e) v[e] = (n0 + e < N && lane < N) ? __ldg(base + (int64_t)(n0 + e) * N + lane) : 0.f;
 #pragma unroll
-  for (int n = 0; n < kNP; ++n) {
-    const uint32_t row = __ballot_sync(0xffffffffu, v[n] > 0.5f);
-    if (lane == n) mine = row;
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t row = __ballot_sync(0xffffffffu, v[e] > 0.5f);
+      if (lane == n0 + e) mine = row;
+    }
   }
   return mine;
 }
@@ -273,61 +277,71 @@ __device__ __forceinline__ int part_channel(int p, int hk, int Hk, int R) {
 
 // Per-unit masks and gates of unit u into buffer buf, by warps 13-15 (warp
 // 15: ancestor masks and conv taps; warps 13, 14: gates of v-head warp - 13).
+// Every global load is issued before any of their values is used.
 template <int R, bool CONV>
 __device__ __forceinline__ void prep_unit(const dft_gdn_args& a, const dft_gdn_conv_args& cv, Small& sm,
                                           int32_t* status, int u, int buf, int warp, int lane) {
   const int N = a.N, Hk = a.Hk;
-    const int b = u / Hk, hk = u % Hk;
-    {
-      const int n = lane;
-      const uint32_t m = anc_mask_warp(a.anc, b, N, lane);
-      if (warp == 15) {
-        sm.anc[buf][n] = m;
-        if (CONV) {
-          uint32_t packed = 0;
-          if (n < N) {
-            const int64_t* ci = cv.cidx + ((int64_t)b * N + n) * 4;
+  const int b = u / Hk, hk = u % Hk;
+  const int n = lane;
+  const int hl = warp - 13, h = hk * R + hl;
+  const bool gate = warp < 15 && hl < R && n < N;
+  // gate inputs (raw bits) and conv columns first
+  uint32_t ra = 0, rb = 0, rd = 0;
+  float dec = 0.f;
+  if (gate) {
+    const int64_t ab = (int64_t)b * a.ab_sb + (int64_t)n * a.ab_sn + h;
+    ra = ld_bits(a.a, a.ab_dtype, ab);
+    rb = ld_bits(a.bg, a.ab_dtype, ab);
+    rd = ld_bits(a.dt_bias, a.dtb_dtype, h);
+    dec = a.neg_exp_A ? __ldg(a.neg_exp_A + h) : -expf(__ldg(a.A_log + h));
+  }
+  int64_t c4[4] = {0, 0, 0, 0};
+  if (CONV && warp == 15 && n < N) {
+    const int64_t* ci = cv.cidx + ((int64_t)b * N + n) * 4;
 #pragma unroll
-            for (int j = 0; j < 3; ++j) {
-              int64_t c = ci[j];
-              if (c < 0 || c >= 3 + N) {
-                raise_status(status, DFT_DEV_BAD_INDEX);
-                c = 3 + n;
-              }
-              packed |= (uint32_t)c << (8 * j);
-            }
-            if (ci[3] != 3 + n) raise_status(status, DFT_DEV_BAD_INDEX);   // tap 3 is the node itself
+    for (int j = 0; j < 4; ++j) c4[j] = __ldg(reinterpret_cast<const long long*>(ci) + j);
+  }
+  const uint32_t m = anc_mask_warp(a.anc, b, N, lane);
+  if (warp == 15) {
+    sm.anc[buf][n] = m;
+    if (CONV) {
+      uint32_t packed = 0;
+      if (n < N) {
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          int64_t c = c4[j];
+          if (c < 0 || c >= 3 + N) {
+            raise_status(status, DFT_DEV_BAD_INDEX);
+            c = 3 + n;
           }
-          sm.taps[buf][n] = packed;
+          packed |= (uint32_t)c << (8 * j);
         }
-      } else if (warp - 13 < R) {
-        // g, beta, G = sum of g over the ancestors in ascending order (tree_kernels.py:146-153)
-        const int hl = warp - 13, h = hk * R + hl;
-        float g = 0.f, beta = 0.f;
-        if (n < N) {
-          // raw loads first, conversions after (one memory round trip)
-          const int64_t ab = (int64_t)b * a.ab_sb + (int64_t)n * a.ab_sn + h;
-          const uint32_t ra = ld_bits(a.a, a.ab_dtype, ab), rb = ld_bits(a.bg, a.ab_dtype, ab);
-          const uint32_t rd = ld_bits(a.dt_bias, a.dtb_dtype, h);
-          const float dec = a.neg_exp_A ? __ldg(a.neg_exp_A + h) : -expf(__ldg(a.A_log + h));
-          const float ar = bits_f32(ra, a.ab_dtype) + bits_f32(rd, a.dtb_dtype);
-          const float sp = ar > 20.f ? ar : logf(1.f + expf(fminf(ar, 20.f)));
-          g = dec * sp;
-          beta = 1.f / (1.f + expf(-bits_f32(rb, a.ab_dtype)));
-        }
-        float G = 0.f;
-#pragma unroll 1
-        for (int j = 0; j < kNP; ++j) {
-          const float gj = __shfl_sync(0xffffffffu, g, j);
-          if ((m >> j) & 1u) G += gj;
-        }
-        sm.G[buf][hl][n] = G;
-        sm.beta[buf][hl][n] = beta;
-        sm.eG[buf][hl][n] = expf(G);
-        if (a.aux_g && n < N) a.aux_g[(int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh + n] = G;
+        if (c4[3] != 3 + n) raise_status(status, DFT_DEV_BAD_INDEX);   // tap 3 is the node itself
       }
-      __syncwarp();
+      sm.taps[buf][n] = packed;
     }
+  } else if (hl < R) {
+    // g, beta, G = sum of g over the ancestors in ascending order (tree_kernels.py:146-153)
+    float g = 0.f, beta = 0.f;
+    if (gate) {
+      const float ar = bits_f32(ra, a.ab_dtype) + bits_f32(rd, a.dtb_dtype);
+      const float sp = ar > 20.f ? ar : logf(1.f + expf(fminf(ar, 20.f)));
+      g = dec * sp;
+      beta = 1.f / (1.f + expf(-bits_f32(rb, a.ab_dtype)));
+    }
+    float G = 0.f;
+#pragma unroll 8
+    for (int j = 0; j < kNP; ++j) {
+      const float gj = __shfl_sync(0xffffffffu, g, j);
+      if ((m >> j) & 1u) G += gj;
+    }
+    sm.G[buf][hl][n] = G;
+    sm.beta[buf][hl][n] = beta;
+    sm.eG[buf][hl][n] = expf(G);
+    if (a.aux_g && n < N) a.aux_g[(int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh + n] = G;
+  }
+  __syncwarp();
 }
 
 template <int R, bool CONV>
@@ -597,19 +611,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
         }
         mma_commit(bar_m1[0]);
-        if (R == 2) {
-          if (!mbar_wait(bar_s1, s1_used & 1)) atomicExch(&sm.abort, 1);
-          ++s1_used;
-          tc_fence_after();
-  #pragma unroll 1
-          for (int kb = 0; kb < 4; ++kb) {
-            const uint64_t da = sw128_desc(sbase + OFF_RT + kb * 16384);
-            const uint64_t db = sw128_desc(sbase + OFF_KQ + kb * 8192);
-  #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1 + 64, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
-          }
-          mma_commit(bar_m1[1]);
-        }
       }
       __syncwarp();   // the control warp reconverges before the next CTA barrier
     }
@@ -677,15 +678,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           r[28 - 4 * c] = q.w;
         }
       }
+      // row i of L in 16-byte chunks: entries at and above the diagonal are
+      // zero (L is strictly lower triangular), so whole chunks can be used
 #pragma unroll
       for (int i = 1; i < 32; ++i) {
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
         for (int m = 0; m < i; m += 4) {
-          s0 = fmaf(L[sq32(i, m)], r[m], s0);
-          if (m + 1 < i) s1 = fmaf(L[sq32(i, m + 1)], r[m + 1], s1);
-          if (m + 2 < i) s2 = fmaf(L[sq32(i, m + 2)], r[m + 2], s2);
-          if (m + 3 < i) s3 = fmaf(L[sq32(i, m + 3)], r[m + 3], s3);
+          const float4 l4 = *reinterpret_cast<const float4*>(L + sq32(i, m));
+          s0 = fmaf(l4.x, r[m], s0);
+          s1 = fmaf(l4.y, r[m + 1], s1);
+          s2 = fmaf(l4.z, r[m + 2], s2);
+          s3 = fmaf(l4.w, r[m + 3], s3);
         }
         r[i] = r[i] - ((s0 + s1) + (s2 + s3));
       }
@@ -717,6 +721,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(xzl + off) = lo;
         }
       }
+    }
+    if (ctl_warp) {
+      if (lane == 0) {
+        // head 0's M1 has long retired: its slot takes the next unit's head-0 state
+        const int nu = u + gridDim.x;
+        if (nu < units) {
+          if (!mbar_wait(bar_m1[0], ph)) atomicExch(&sm.abort, 1);
+          issue_state(nu, 0);
+          ++s_issued;
+        }
+        if (R == 2) {
+          // head 1's M1 (its state streamed into the R^T region between units)
+          if (!mbar_wait(bar_s1, s1_used & 1)) atomicExch(&sm.abort, 1);
+          ++s1_used;
+          tc_fence_after();
+          const uint32_t id1 = idesc_tf32(128, 64);
+  #pragma unroll 1
+          for (int kb = 0; kb < 4; ++kb) {
+            const uint64_t da = sw128_desc(sbase + OFF_RT + kb * 16384);
+            const uint64_t db = sw128_desc(sbase + OFF_KQ + kb * 8192);
+  #pragma unroll
+            for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1 + 64, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
+          }
+          mma_commit(bar_m1[1]);
+        }
+      }
+      __syncwarp();   // the control warp reconverges before its E1 (warp-collective TMEM loads)
     }
     // ------------------------------------------------ E1 (warps 8-15), alongside the X / Z solves
     if (warp >= 8 && ((warp - 8) >> 2) < R) {
@@ -755,12 +786,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (sm.abort) break;
     if (ctl_warp) {
       if (lane == 0) {
-        // every M1 of this unit has retired and the tile is consumed: request the next unit's
+        // the tile is consumed: request the next unit's
         const int nu = u + gridDim.x;
         if (nu < units) {
-          issue_act(nu);        // needed first (the next unit's conv)
-          issue_state(nu, 0);   // needed at its M1
-          ++s_issued;
+          issue_act(nu);
           ++x_issued;
         }
         // M2 per head: D2 = R^T [X; Z]^T, 3xTF32 (hi.hi + hi.lo + lo.hi)
@@ -778,20 +807,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, al + 2 * ks, bh + 2 * ks, id2, 1);
           mma_commit(bar_m2[hh]);
         }
+        if (R == 2 && nu < units) {
+          // once M2 has read R^T, the region takes the next unit's head-1 state
+          if (!mbar_wait(bar_m2[R - 1], ph)) atomicExch(&sm.abort, 1);
+          issue_state(nu, 1);
+          ++s1_issued;
+        }
       }
       __syncwarp();   // the control warp reconverges before the next CTA barrier
     }
     // ------------------------------------------------ E2: vn and o = e^G (q S0) + Z R
-    // thread v stages column v of vn / o over R^T (read by M2); then each of the
-    // head's four warps stores eight rows with coalesced 16-byte stores
+    // thread v holds column v: for each node row a warp writes 32 consecutive
+    // elements (128 bytes of vn, 64 bytes of o); no shared-memory staging, so
+    // the R^T region is free once M2 has read it
     if (warp >= 8 && ((warp - 8) >> 2) < R) {
       const int hh = (warp - 8) >> 2;
       if (!mbar_wait(bar_m2[hh], ph)) atomicExch(&sm.abort, 1);
       tc_fence_after();
       const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
       const int h = hk * R + hh, v = tid & 127;
-      float* vst = reinterpret_cast<float*>(smem + OFF_RT + hh * 32768);            // [n][128] f32
-      T* ost = reinterpret_cast<T*>(smem + OFF_RT + hh * 32768 + 16384);            // [n][128] bf16
+      float* gv = a.aux_vn ? a.aux_vn + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh + v : nullptr;
+      T* go = reinterpret_cast<T*>(a.o) + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + v;
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
         float vn[16], zr[16], qs[16];
@@ -801,28 +837,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int n = 16 * half + e;
-          vst[n * kD + v] = vn[e];
-          ost[n * kD + v] = __float2bfloat16_rn(sm.eG[cb][hh][n] * qs[e] + zr[e]);
-        }
-      }
-      named_bar(1 + hh, 128);
-      const int r0 = 8 * (warp & 3);
-      if (a.aux_vn) {
-        float* g = a.aux_vn + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh + lane * 4;
-#pragma unroll 4
-        for (int e = 0; e < 8; ++e) {
-          const int n = r0 + e;
-          if (n < N)
-            *reinterpret_cast<float4*>(g + (int64_t)n * a.av_sn) = *reinterpret_cast<const float4*>(vst + n * kD + lane * 4);
-        }
-      }
-      {
-        T* g = reinterpret_cast<T*>(a.o) + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + (lane & 15) * 8;
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const int n = r0 + e + (lane >> 4);   // lanes 0-15 one row, 16-31 the next
-          if (n < N)
-            *reinterpret_cast<uint4*>(g + (int64_t)n * a.o_sn) = *reinterpret_cast<const uint4*>(ost + n * kD + (lane & 15) * 8);
+          if (n < N) {
+            if (gv) gv[(int64_t)n * a.av_sn] = vn[e];
+            go[(int64_t)n * a.o_sn] = __float2bfloat16_rn(sm.eG[cb][hh][n] * qs[e] + zr[e]);
+          }
         }
       }
     }
@@ -830,17 +848,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     if (sm.abort) break;
-    if (ctl_warp) {
-      if (R == 2 && lane == 0) {
-        // the staging in the R^T region has been read: the next unit's head-1 state goes there
-        const int nu = u + gridDim.x;
-        if (nu < units) {
-          issue_state(nu, 1);
-          ++s1_issued;
-        }
-      }
-      __syncwarp();   // the control warp reconverges before the next CTA barrier
-    }
   }
   // ------------------------------------------------ teardown
   __syncthreads();
