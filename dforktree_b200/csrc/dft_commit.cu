@@ -18,7 +18,7 @@ constexpr int kD = 128;
 constexpr int kThreads = 256;
 constexpr int kMaxPath = 64;
 
-__global__ void __launch_bounds__(kThreads) gdn_commit_kernel(dft_commit_args a, int32_t* st) {
+__global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args a, int32_t* st) {
   extern __shared__ __align__(16) float s_path[];  // [cap][kD] k*w, then [cap][kD] vn
   __shared__ int s_ids[kMaxPath];
   __shared__ float s_w[kMaxPath];
@@ -43,24 +43,50 @@ __global__ void __launch_bounds__(kThreads) gdn_commit_kernel(dft_commit_args a,
   const int khead = a.aux_k_per_v ? h : h / R;
   const float* G = a.aux_g + (int64_t)l * a.ag_sl + (int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh;
   const float gu = G[u];
-  if (tid == 0) {
-    // path nodes that are ancestors-or-self of u, in path order (fc1_fused.py:30-35)
-    int n = 0;
+  const int64_t slot = a.slots_in ? a.slots_in[b] : b;
+  const int64_t dst = a.slots_out ? a.slots_out[b] : b;
+  const float* S0 = a.state_in + (int64_t)l * a.si_sl + slot * a.si_ss + (int64_t)h * a.si_sh;
+  float* So = a.state_out + (int64_t)l * a.so_sl + dst * a.so_ss + u * a.so_su + (int64_t)h * a.so_sh;
+  const int k4 = (tid & 31) * 4;
+  const int v0 = tid >> 5;  // rows v0, v0 + 8, ..., 16 rows per thread
+  const bool vec = a.si_sk == 1 && a.so_sk == 1 && (a.si_sv % 4 == 0) && (a.so_sv % 4 == 0) &&
+                   ((uintptr_t)S0 % 16 == 0) && ((uintptr_t)So % 16 == 0);
+  // the state tile does not depend on the path: its loads go out first and
+  // overlap the path set-up below
+  float4 acc[16];
+  if (vec) {
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = __ldcs(reinterpret_cast<const float4*>(S0 + (int64_t)(v0 + 8 * r) * a.si_sv + k4));
+  } else {
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const float* p = S0 + (int64_t)(v0 + 8 * r) * a.si_sv + (int64_t)k4 * a.si_sk;
+      acc[r] = make_float4(p[0], p[a.si_sk], p[2 * a.si_sk], p[3 * a.si_sk]);
+    }
+  }
+  if (tid < 32) {
+    // path nodes that are ancestors-or-self of u, in path order (fc1_fused.py:30-35):
+    // lane t looks at path entries t and t + 32, a ballot compacts them in order
     const float* anc_u = a.anc + ((int64_t)b * a.N + u) * a.N;
-    for (int t = 0; t < a.P; ++t) {
-      const int64_t id = a.path[(int64_t)b * a.P + t];
-      if (id < 0) continue;
+    const int cap_n = a.P < a.N ? a.P : a.N;
+    int base = 0;
+    for (int t0 = 0; t0 < a.P; t0 += 32) {
+      const int t = t0 + tid;
+      int64_t id = t < a.P ? a.path[(int64_t)b * a.P + t] : -1;
       if (id >= a.N) {
         raise_status(st, DFT_DEV_BAD_INDEX);
-        continue;
+        id = -1;
       }
-      if (anc_u[id] > 0.f && n < a.P && n < a.N) {
-        s_ids[n] = (int)id;
-        s_w[n] = expf(gu - G[id]);
-        ++n;
+      const bool keep = id >= 0 && anc_u[id] > 0.f;
+      const uint32_t m = __ballot_sync(0xffffffffu, keep);
+      const int pos = base + __popc(m & ((1u << tid) - 1u));
+      if (keep && pos < cap_n) {
+        s_ids[pos] = (int)id;
+        s_w[pos] = expf(gu - G[id]);
       }
+      base += __popc(m);
     }
-    s_n = n;
+    if (tid == 0) s_n = base < cap_n ? base : cap_n;
   }
   __syncthreads();
   const int np = s_n;
@@ -75,26 +101,7 @@ __global__ void __launch_bounds__(kThreads) gdn_commit_kernel(dft_commit_args a,
     skk[t][d] = Kb[(int64_t)id * a.ak_sn + d] * s_w[t];  // (k * w) (fc1_fused.py:39)
     svv[t][d] = Vb[(int64_t)id * a.av_sn + d];
   }
-  const int64_t slot = a.slots_in ? a.slots_in[b] : b;
-  const int64_t dst = a.slots_out ? a.slots_out[b] : b;
-  const float* S0 = a.state_in + (int64_t)l * a.si_sl + slot * a.si_ss + (int64_t)h * a.si_sh;
-  float* So = a.state_out + (int64_t)l * a.so_sl + dst * a.so_ss + u * a.so_su + (int64_t)h * a.so_sh;
   const float eg = expf(gu);
-  const int k4 = (tid & 31) * 4;
-  const int v0 = tid >> 5;  // rows v0, v0 + 8, ..., 16 rows per thread
-  const bool vec = a.si_sk == 1 && a.so_sk == 1 && (a.si_sv % 4 == 0) && (a.so_sv % 4 == 0) &&
-                   ((uintptr_t)S0 % 16 == 0) && ((uintptr_t)So % 16 == 0);
-  float4 acc[16];
-  if (vec) {
-#pragma unroll
-    for (int r = 0; r < 16; ++r) acc[r] = __ldcs(reinterpret_cast<const float4*>(S0 + (int64_t)(v0 + 8 * r) * a.si_sv + k4));
-  } else {
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const float* p = S0 + (int64_t)(v0 + 8 * r) * a.si_sv + (int64_t)k4 * a.si_sk;
-      acc[r] = make_float4(p[0], p[a.si_sk], p[2 * a.si_sk], p[3 * a.si_sk]);
-    }
-  }
   __syncthreads();
 #pragma unroll
   for (int r = 0; r < 16; ++r) {

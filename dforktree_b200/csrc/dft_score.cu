@@ -124,6 +124,14 @@ __global__ void __launch_bounds__(kThreads) score_kernel(const T* __restrict__ l
   L.thr = -INFINITY;
   L.thr_i = INT_MAX;
   float m = -INFINITY, sum = 0.f;
+  // Block-wide pruning bound: each warp list holds 16 values >= its 16th, so no
+  // value below the largest warp 16th can reach the row's top 16.  Warps publish
+  // their 16th after every sweep and offer only values >= the largest published
+  // one (thresholds only rise, so any stale read is still a valid bound).
+  __shared__ float s_thr[kWarps];
+  if (lane == 0) s_thr[warp] = -INFINITY;
+  __syncthreads();
+  float bound = -INFINITY;
 
   // scalar head up to 16-byte alignment, vector body, scalar tail
   int head = (int)((((uintptr_t)x + 15) & ~(uintptr_t)15) - (uintptr_t)x) / (int)sizeof(T);
@@ -143,8 +151,13 @@ __global__ void __launch_bounds__(kThreads) score_kernel(const T* __restrict__ l
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       float mx = fmaxf(fmaxf(vs[r].x, vs[r].y), fmaxf(vs[r].z, vs[r].w));
-      offer4(L, mx >= L.thr, vs[r], (int)(e + r * stride), lane);
+      offer4(L, mx >= L.thr && mx >= bound, vs[r], (int)(e + r * stride), lane);
     }
+    if (lane == 0) reinterpret_cast<volatile float*>(s_thr)[warp] = L.thr;
+    float t = reinterpret_cast<volatile float*>(s_thr)[lane & (kWarps - 1)];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+    bound = fmaxf(bound, t);
   }
   for (; base < body_end; base += stride) {
     const int64_t e = base + (int64_t)tid * 4;
