@@ -72,7 +72,9 @@ struct Small {
   uint32_t anc[2][kNP];            // bit j: j is i or an ancestor of i
   uint32_t taps[2][kNP];           // tile rows of conv taps 0..2 (one byte each; tap 3 is the node)
   __align__(16) float G[2][2][kNP];   // [buffer][v-head][node]
-  float beta[2][2][kNP], eG[2][2][kNP];
+  __align__(16) float beta[2][2][kNP];
+  __align__(16) float eG[2][2][kNP];
+  int s1_issued;                   // head-1 state loads requested (any thread that issues one)
 };
 static_assert(sizeof(Small) <= kSmallBytes, "small region");
 
@@ -216,8 +218,8 @@ __device__ __forceinline__ float bits_f32(uint32_t v, int dtype) {
 __device__ __forceinline__ uint32_t anc_mask_warp(const float* anc, int b, int N, int lane) {
   uint32_t mine = 0;
   const float* base = anc + (int64_t)b * N * N;
-  // eight rows in flight per step
-#pragma unroll 1
+  // eight rows per step, two steps in flight
+#pragma unroll 2
   for (int n0 = 0; n0 < kNP; n0 += 8) {
     float v[8];
 #pragma unroll
@@ -387,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_dr, 1);
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
       sm.abort = 0;
+      sm.s1_issued = 0;
     }
     __syncwarp();   // the control warp reconverges before the next CTA barrier
   }
@@ -424,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   once);
   };
   // control-thread bookkeeping for the drain on timeout
-  int s_issued = 0, s_used = 0, s1_issued = 0, s1_used = 0, x_issued = 0, x_used = 0;
+  int s_issued = 0, s_used = 0, s1_used = 0, x_issued = 0, x_used = 0;
   if (ctl_warp) {
     if (lane == 0 && (int)blockIdx.x < units) {
       issue_act(blockIdx.x);
@@ -433,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       x_issued = 1;
       if (R == 2) {
         issue_state(blockIdx.x, 1);
-        s1_issued = 1;
+        sm.s1_issued = 1;
       }
     }
     __syncwarp();   // the control warp reconverges before the next CTA barrier
@@ -767,10 +770,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         float4 hi, lo;
         float* phi = &hi.x;
         float* plo = &lo.x;
+        const float4 be4 = *reinterpret_cast<const float4*>(&sm.beta[cb][hh][4 * c]);
+        const float4 eg4 = *reinterpret_cast<const float4*>(&sm.eG[cb][hh][4 * c]);
+        const float* be = &be4.x;
+        const float* eg = &eg4.x;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int n = 4 * c + e;
-          const float rr = sm.beta[cb][hh][n] * (to_f32(yv[n * kD]) - sm.eG[cb][hh][n] * ks_[n]);
+          const float rr = be[e] * (to_f32(yv[n * kD]) - eg[e] * ks_[n]);
           phi[e] = tf32_rna(rr);
           plo[e] = tf32_rna(rr - phi[e]);
         }
@@ -807,14 +814,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, al + 2 * ks, bh + 2 * ks, id2, 1);
           mma_commit(bar_m2[hh]);
         }
-        if (R == 2 && nu < units) {
-          // once M2 has read R^T, the region takes the next unit's head-1 state
-          if (!mbar_wait(bar_m2[R - 1], ph)) atomicExch(&sm.abort, 1);
-          issue_state(nu, 1);
-          ++s1_issued;
-        }
       }
       __syncwarp();   // the control warp reconverges before the next CTA barrier
+    }
+    if (R == 2 && warp == 0) {
+      if (lane == 0) {
+        // once M2 has read R^T, the region takes the next unit's head-1 state
+        const int nu = u + gridDim.x;
+        if (nu < units) {
+          if (!mbar_wait(bar_m2[R - 1], ph)) atomicExch(&sm.abort, 1);
+          issue_state(nu, 1);
+          ++sm.s1_issued;
+        }
+      }
+      __syncwarp();
     }
     // ------------------------------------------------ E2: vn and o = e^G (q S0) + Z R
     // thread v holds column v: for each node row a warp writes 32 consecutive
@@ -835,11 +848,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem + lanes + COL_M2 + 64 * hh + 32 + 16 * half, zr);
         tmem_ld16(tmem + lanes + COL_M1 + 64 * hh + 32 + 16 * half, qs);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int n = 16 * half + e;
-          if (n < N) {
-            if (gv) gv[(int64_t)n * a.av_sn] = vn[e];
-            go[(int64_t)n * a.o_sn] = __float2bfloat16_rn(sm.eG[cb][hh][n] * qs[e] + zr[e]);
+        for (int e4 = 0; e4 < 16; e4 += 4) {
+          const float4 eg4 = *reinterpret_cast<const float4*>(&sm.eG[cb][hh][16 * half + e4]);
+          const float* eg = &eg4.x;
+#pragma unroll
+          for (int e = e4; e < e4 + 4; ++e) {
+            const int n = 16 * half + e;
+            if (n < N) {
+              if (gv) gv[(int64_t)n * a.av_sn] = vn[e];
+              go[(int64_t)n * a.o_sn] = __float2bfloat16_rn(eg[e - e4] * qs[e] + zr[e]);
+            }
           }
         }
       }
@@ -857,7 +875,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         raise_status(status, DFT_DEV_TIMEOUT);
         // drain what this CTA issued before freeing its shared memory / TMEM (bounded)
         for (; s_used < s_issued; ++s_used) mbar_wait(bar_s, s_used & 1);
-        for (; s1_used < s1_issued; ++s1_used) mbar_wait(bar_s1, s1_used & 1);
+        for (; s1_used < sm.s1_issued; ++s1_used) mbar_wait(bar_s1, s1_used & 1);
         for (; x_used < x_issued; ++x_used) mbar_wait(bar_x, x_used & 1);
         mma_commit(bar_dr);   // arrives once every MMA this thread issued has retired
         mbar_wait(bar_dr, 0);
