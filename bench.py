@@ -140,49 +140,86 @@ class CpuSampler:
 
 # ------------------------------------------------------------- clocks ------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons of this rank's GPU, sampled every 20 ms
+    in a background thread through NVML (read-only queries), for the duration of
+    the timed region; the GPU is identified by its UUID, so the sample follows
+    the device this process runs on whatever CUDA_VISIBLE_DEVICES maps.  Falls
+    back to `nvidia-smi -i <uuid>` when NVML is unavailable."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = None
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.rows = []          # (sm_mhz, max_mhz, set of reasons)
+        self._stop = None
+        self._thread = None
+
+    def _uuid(self):
+        import torch
+        u = str(torch.cuda.get_device_properties(self.device_index).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
 
     def __enter__(self):
+        import threading
+        self._stop = threading.Event()
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByUUID(self._uuid())
+            bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+
+            def sample():
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((float(sm), float(mx), {k for k, b in bits.items() if r & b}))
         except Exception:
-            self.proc = None
+            sample = self._smi_sampler()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    sample()
+                except Exception:
+                    pass
+                self._stop.wait(0.02)
+
+        if sample is not None:
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
         return self
 
-    def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(5)
-            except Exception:
-                self.proc.kill()
-
-    def summary(self):
+    def _smi_sampler(self):
         try:
-            rows = [r.split(",") for r in open(self.path).read().strip().split("\n") if r.strip()]
-            os.unlink(self.path)
+            uuid = self._uuid()
         except Exception:
             return None
-        rows = [[x.strip() for x in r] for r in rows if len(r) >= 9]
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_power_cap")
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+
+        def sample():
+            out = subprocess.run(["nvidia-smi", "-i", uuid, f"--query-gpu={fields}", "--format=csv,noheader,nounits"],
+                                 capture_output=True, text=True, timeout=5).stdout.strip().split(",")
+            out = [x.strip() for x in out]
+            self.rows.append((float(out[0]), float(out[1]),
+                              {names[i] for i in range(4) if out[2 + i].lower() == "active"}))
+        return sample
+
+    def __exit__(self, *exc):
+        if self._stop is not None:
+            self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def summary(self):
+        if not self.rows:
+            return None
+        sm = [r[0] for r in self.rows]
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[1] for r in self.rows),
+                "reasons": sorted(set().union(*[r[2] for r in self.rows])), "samples": len(self.rows)}
 
 
 # ---------------------------------------------------------------- ours -----
