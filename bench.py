@@ -34,7 +34,7 @@ WORKLOAD = ("dforktree cycle: batch 64/GPU, S=24, V=248320 fp32 logits, 2M+8M n-
             "greedy accept (len U[1,24]), in-place commit")
 S, V, N, M, LAYERS, HK, HV, D = 24, 248320, 32, 16, 24, 16, 32, 128
 C_CONV = 2 * HK * D + HV * D
-# algorithmic bytes per unit (per layer-request), see DESIGN.md
+# algorithmic bytes per unit (per layer-request): state in, q / k / v in, gates, o out
 VERIFY_BYTES = 2 * 1024 * 1024 + 262144 + 262144 + 8192 + 262144      # S0 + q,k + v + g,beta + o
 # the fused launch also reads the conv state / weights and writes the aux rows the commit needs
 VERIFY_AUX_BYTES = 8192 * 3 * 2 + 262144 + 524288 + 4096               # conv state + k_hat + vn + G
@@ -278,7 +278,7 @@ def run_ours(args, rank, world, local_rank):
         ev["v1"].record(stream)
         cyc.accept(target_fn(cyc.tree))
         ev["c0"].record(stream)
-        cyc.commit()
+        cyc.commit(x)
         ev["c1"].record(stream)
 
     for _ in range(args.warmup):
@@ -316,7 +316,7 @@ def run_ours(args, rank, world, local_rank):
             e2.record(stream)
             pairs.append((e1, e2))
         cyc.accept(target_fn(cyc.tree))
-        cyc.commit()
+        cyc.commit(x)
     torch.cuda.synchronize()
     for e1, e2 in pairs:
         verify_ms += e1.elapsed_time(e2)

@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(_HERE, "libdforktree_b200.so")
 
 DFT_F32, DFT_BF16, DFT_F16 = 0, 1, 2
 DFT_OK, DFT_ERR_INVALID, DFT_ERR_UNSUPPORTED = 0, 1, 2
+DFT_ERR_TABLE, DFT_ERR_IO = 4, 7
 DEV_BAD_TOKEN, DEV_PROBE_LIMIT, DEV_BAD_INDEX, DEV_TIMEOUT = 1, 2, 4, 8
 
 _DTYPES = {torch.float32: DFT_F32, torch.bfloat16: DFT_BF16, torch.float16: DFT_F16}
@@ -24,7 +25,9 @@ i32, i64, f32, vp = C.c_int32, C.c_int64, C.c_float, C.c_void_p
 
 
 class DFTError(RuntimeError):
-    pass
+    def __init__(self, msg, status=None):
+        super().__init__(msg)
+        self.status = status
 
 
 class TableDesc(C.Structure):
@@ -60,6 +63,13 @@ class ConvArgs(C.Structure):
                 ("y", vp), ("y_dtype", i32), ("y_sb", i64), ("y_sn", i64),
                 ("iw", vp), ("iw_dtype", i32), ("iw_sd", i64), ("iw_sn", i64), ("iw_sc", i64), ("iw_sj", i64),
                 ("iw_slots", vp)]
+
+
+class ConvCommitArgs(C.Structure):
+    _fields_ = [("L", i32), ("B", i32), ("N", i32), ("C", i32),
+                ("x", vp), ("x_dtype", i32), ("x_sl", i64), ("x_sb", i64), ("x_sn", i64),
+                ("conv_state", vp), ("cs_dtype", i32), ("cs_sl", i64), ("cs_ss", i64), ("cs_sc", i64), ("cs_st", i64),
+                ("slots", vp), ("cidx", vp), ("last", vp)]
 
 
 class GdnConvArgs(C.Structure):
@@ -106,6 +116,10 @@ SIGNATURES = {
     "dft_table_destroy": (C.c_int, [vp]),
     "dft_table_info": (C.c_int, [vp, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64), C.POINTER(i64),
                                  C.POINTER(i64)]),
+    "dft_table_set_params": (C.c_int, [vp, f32, f32, f32, f32]),
+    "dft_table_copy_marginals": (C.c_int, [vp, vp, vp, vp]),
+    "dft_table_save": (C.c_int, [vp, C.c_char_p, vp]),
+    "dft_table_load": (C.c_int, [C.c_char_p, C.POINTER(vp), vp]),
     "dft_ngram_eval": (C.c_int, [vp, C.c_int, C.c_int, vp, vp, vp, vp, i64, vp, vp, vp]),
     "dft_score": (C.c_int, [C.POINTER(BuildParams), vp, i32, i64, i64, vp, vp, vp, vp]),
     "dft_pmi_dense": (C.c_int, [vp, C.POINTER(BuildParams), vp, vp, vp, vp, vp, vp]),
@@ -119,6 +133,7 @@ SIGNATURES = {
     "dft_tree_struct": (C.c_int, [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
     "dft_accept_greedy": (C.c_int, [i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "dft_tree_conv": (C.c_int, [C.POINTER(ConvArgs), vp, vp]),
+    "dft_conv_commit": (C.c_int, [C.POINTER(ConvCommitArgs), vp, vp]),
     "dft_gdn_tree_verify": (C.c_int, [C.POINTER(GdnArgs), vp, vp]),
     "dft_gdn_commit": (C.c_int, [C.POINTER(CommitArgs), vp, vp]),
 }
@@ -154,7 +169,7 @@ def lib():
 def check(rc: int, what: str):
     if rc != 0:
         msg = load().dft_status_string(rc).decode()
-        raise DFTError(f"{what} failed: {msg} (status {rc})")
+        raise DFTError(f"{what} failed: {msg} (status {rc})", rc)
 
 
 def dtype_code(t: torch.Tensor) -> int:

@@ -40,6 +40,7 @@ extern "C" const char* dft_status_string(int s) {
     case DFT_ERR_TABLE: return "n-gram table keys unsorted, negative or table full";
     case DFT_ERR_NO_DEVICE: return "no sm_100 device";
     case DFT_ERR_CAPACITY: return "shape exceeds the static scratch of dft_score_build_static (32 MiB)";
+    case DFT_ERR_IO: return "table file missing, unwritable, truncated or damaged";
     default: return "unknown status";
   }
 }

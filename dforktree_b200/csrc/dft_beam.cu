@@ -1,4 +1,4 @@
-// Fork-aware beam tree search and tree structure.
+// Fork-aware beam tree search and tree structure (tree_ops.py:7-89, fc1_builder.py:30-47).
 //
 // Reference: tree_ops.beam_tree (tree_ops.py:7-53) runs ~20 torch ops per
 // step plus a global top-(N-1); tree_ops.tree_struct (tree_ops.py:68-89)

@@ -1,4 +1,4 @@
-// Closed-form commit of the accepted path's recurrent state.
+// Closed-form commit of the accepted path's recurrent state (fc1_fused.py:27-49).
 // Reference: fc1_fused.snapshots (fc1_fused.py:27-49): for each layer, head
 // and end node u,
 //   S_u = e^{G_u} S0 + sum_{t in path, t anc-or-self of u} e^{G_u - G_t} k_t vn_t^T

@@ -1,4 +1,4 @@
-// Tree-aware causal depthwise conv.
+// Tree-aware causal depthwise conv (fc1_conv.py:8-27, tree_kernels.py:17-33).
 // Reference: fc1_conv.conv (fc1_conv.py:8-27) and tree_kernels._tree_conv_kernel
 // (tree_kernels.py:17-33): y[n, c] = SiLU(sum_j w[c, j] * x_j + bias[c]) where
 // tap j reads conv column cidx[n, j] -- columns 0..2 are the conv state, 3+m
@@ -52,6 +52,53 @@ extern "C" int dft_tree_conv(const dft_conv_args* a, int32_t* dev_status, void* 
     return DFT_ERR_INVALID;
   dim3 grid((a->C + 255) / 256, a->N, a->B);
   tree_conv_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*a, dev_status);
+  DFT_LAUNCH_CHECK();
+  return DFT_OK;
+}
+
+// ------------------------------------------------------ conv-window commit --
+// conv_state[l, slot(b), c, j] <- input at column cidx[b, u, j + 1], u = last[b]:
+// the window of the last accepted node (fc1_conv.py:22-27 writes the same taps
+// into intermediate_conv_window; SGLang's commit copies them into the state).
+// One thread per (channel, request, layer); the three values are read before
+// any is written, so the update is in place.
+namespace {
+
+__global__ void conv_commit_kernel(dft_conv_commit_args a, int32_t* st) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y, l = blockIdx.z;
+  if (c >= a.C) return;
+  const int64_t u = a.last[b];
+  if (u < 0) return;
+  if (u >= a.N) {
+    if (c == 0) raise_status(st, DFT_DEV_BAD_INDEX);
+    return;
+  }
+  const int64_t slot = a.slots ? a.slots[b] : b;
+  const int64_t sbase = (int64_t)l * a.cs_sl + slot * a.cs_ss + (int64_t)c * a.cs_sc;
+  float v[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int64_t col = a.cidx[((int64_t)b * a.N + u) * 4 + j + 1];
+    if (col < 0 || col >= 3 + a.N) {
+      raise_status(st, DFT_DEV_BAD_INDEX);
+      return;
+    }
+    v[j] = col < 3 ? load_any(a.conv_state, a.cs_dtype, sbase + col * a.cs_st)
+                   : load_any(a.x, a.x_dtype, (int64_t)l * a.x_sl + (int64_t)b * a.x_sb + (col - 3) * a.x_sn + c);
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) store_any(a.conv_state, a.cs_dtype, sbase + j * a.cs_st, v[j]);
+}
+
+}  // namespace
+
+extern "C" int dft_conv_commit(const dft_conv_commit_args* a, int32_t* dev_status, void* stream) {
+  if (!a || !a->x || !a->conv_state || !a->cidx || !a->last) return DFT_ERR_INVALID;
+  if (a->L <= 0 || a->B <= 0 || a->N <= 0 || a->C <= 0 || a->B > 65535 || a->L > 65535) return DFT_ERR_INVALID;
+  if (!valid_dtype(a->x_dtype) || !valid_dtype(a->cs_dtype)) return DFT_ERR_INVALID;
+  dim3 grid((a->C + 255) / 256, a->B, a->L);
+  conv_commit_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*a, dev_status);
   DFT_LAUNCH_CHECK();
   return DFT_OK;
 }

@@ -1,4 +1,4 @@
-// Gated-DeltaNet tree verifier.
+// Gated-DeltaNet tree verifier, CUDA-core path (tree_kernels.py:136-208).
 //
 // Reference: tree_gdn_split (tree_kernels.py:193-208) = _tree_prepare
 // (:136-164) -> invert32 (fc1_block_inverse.py:69-78) -> _tree_finish

@@ -1,4 +1,4 @@
-// Drafter-logit scoring (SURVEY row A5, fc1_builder.py:27-28):
+// Drafter-logit scoring (fc1_builder.py:27-28):
 //   lp, ids = topk(log_softmax(logits), M);  rest = log(clamp(1 - sum exp(lp), 1e-6, 1))
 // One CTA streams one [V] row once from HBM (128-bit loads, 4 in flight per
 // thread), keeping per lane an online (max, sum-exp) pair and per warp a

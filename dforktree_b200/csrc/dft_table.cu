@@ -1,4 +1,4 @@
-// n-gram tables in HBM and the PMI lookup kernels.
+// n-gram tables in HBM and the PMI lookup kernels (ngram_gpu.py:8-70).
 //
 // Reference: dforktree/ngram_gpu.py -- sorted int64 key arrays searched with
 // torch.searchsorted (~log2(8M) = 23 dependent HBM reads per query).  Here the
@@ -11,7 +11,9 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <new>
+#include <string>
 
 using namespace dft;
 
@@ -24,6 +26,7 @@ struct dft_table {
   float* pn = nullptr;
   float* n4c = nullptr;
   int64_t pair_slots = 0, trip_slots = 0, quad_slots = 0, bytes = 0;
+  int64_t n4c_len = 0;  // entries of n4c (the trigram count when a quad table exists)
   int device = -1;
 };
 
@@ -100,6 +103,32 @@ int insert(Slot* tab, int64_t slots, const int64_t* keys, const float* vals, int
   return DFT_OK;
 }
 
+// Device view and byte count of a table whose arrays are in place.
+void set_view(dft_table* t, int64_t V, bool has_trip, bool has_quad, bool has_ctx, float beta2, float beta3,
+              float beta4, float clip) {
+  t->bytes = (t->pair_slots + t->trip_slots + t->quad_slots) * (int64_t)sizeof(Slot) +
+             2 * V * (int64_t)sizeof(float) + t->n4c_len * (int64_t)sizeof(float);
+  TableView& v = t->view;
+  v.V = V;
+  v.pair = t->pair;
+  v.pair_mask = (unsigned long long)(t->pair_slots - 1);
+  v.trip = t->trip;
+  v.trip_mask = t->trip_slots ? (unsigned long long)(t->trip_slots - 1) : 0ull;
+  v.quad = t->quad;
+  v.quad_mask = t->quad_slots ? (unsigned long long)(t->quad_slots - 1) : 0ull;
+  v.prev = t->prev;
+  v.pn = t->pn;
+  v.n4c = t->n4c;
+  v.has_pair = 1;
+  v.has_trip = has_trip;
+  v.has_quad = has_quad;
+  v.has_ctx = has_ctx;
+  v.beta2 = beta2;
+  v.beta3 = beta3;
+  v.beta4 = beta4;
+  v.clip = clip;
+}
+
 void free_table(dft_table* t) {
   if (!t) return;
   cudaFree(t->pair);
@@ -173,29 +202,8 @@ extern "C" int dft_table_create(const dft_table_desc* d, dft_table** out, void* 
     }
   }
   cudaFree(err);
-  t->bytes = (t->pair_slots + t->trip_slots + t->quad_slots) * (int64_t)sizeof(Slot) +
-             2 * d->V * (int64_t)sizeof(float) + (d->n_quad ? d->n_trigram * (int64_t)sizeof(float) : 0);
-  {
-    TableView& v = t->view;
-    v.V = d->V;
-    v.pair = t->pair;
-    v.pair_mask = (unsigned long long)(t->pair_slots - 1);
-    v.trip = t->trip;
-    v.trip_mask = t->trip_slots ? (unsigned long long)(t->trip_slots - 1) : 0ull;
-    v.quad = t->quad;
-    v.quad_mask = t->quad_slots ? (unsigned long long)(t->quad_slots - 1) : 0ull;
-    v.prev = t->prev;
-    v.pn = t->pn;
-    v.n4c = t->n4c;
-    v.has_pair = 1;
-    v.has_trip = d->n_trigram > 0;
-    v.has_quad = d->n_quad > 0;
-    v.has_ctx = d->n_ctx3 > 0;
-    v.beta2 = d->beta2;
-    v.beta3 = d->beta3;
-    v.beta4 = d->beta4;
-    v.clip = d->clip;
-  }
+  t->n4c_len = d->n_quad ? d->n_trigram : 0;
+  set_view(t, d->V, d->n_trigram > 0, d->n_quad > 0, d->n_ctx3 > 0, d->beta2, d->beta3, d->beta4, d->clip);
   *out = t;
   return DFT_OK;
 fail:
@@ -223,6 +231,259 @@ extern "C" int dft_table_info(const dft_table* t, int64_t* V, int64_t* ps, int64
 }
 
 const TableView* dft_table_view(const dft_table* t) { return t ? &t->view : nullptr; }
+
+extern "C" int dft_table_set_params(dft_table* t, float beta2, float beta3, float beta4, float clip) {
+  if (!t) return DFT_ERR_INVALID;
+  t->view.beta2 = beta2;
+  t->view.beta3 = beta3;
+  t->view.beta4 = beta4;
+  t->view.clip = clip;
+  return DFT_OK;
+}
+
+extern "C" int dft_table_copy_marginals(const dft_table* t, float* prev, float* pn, void* stream) {
+  if (!t) return DFT_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t n = (size_t)t->view.V * sizeof(float);
+  if (prev && cudaMemcpyAsync(prev, t->prev, n, cudaMemcpyDefault, st) != cudaSuccess) return DFT_ERR_CUDA;
+  if (pn && cudaMemcpyAsync(pn, t->pn, n, cudaMemcpyDefault, st) != cudaSuccess) return DFT_ERR_CUDA;
+  return DFT_OK;
+}
+
+// ------------------------------------------------------- cached table file --
+// The built hash tables as one file: a 128-byte header, then the device images
+// of the pair / triple / quad slot arrays, prev[V], pn[V] and n4c, in that
+// order, little-endian.  Loading is a sequential read plus host-to-device
+// copies (no key sort, no hash insert); the slot images are byte-identical to
+// the saved table's, so every lookup answers the same.  A 64-bit checksum over
+// the payload guards against truncated or damaged files.
+namespace {
+
+constexpr char kMagic[8] = {'D', 'F', 'T', 'T', 'A', 'B', 'L', 'E'};
+constexpr uint32_t kFileVersion = 1;
+constexpr uint32_t kFlagTrip = 1, kFlagQuad = 2, kFlagCtx = 4;
+constexpr size_t kChunk = size_t(32) << 20;  // staging chunk (pinned), multiple of 8
+
+struct FileHeader {
+  char magic[8];
+  uint32_t version, flags;
+  int64_t V, pair_slots, trip_slots, quad_slots, n4c_len;
+  float beta2, beta3, beta4, clip;
+  uint64_t payload_bytes;
+  uint64_t checksum;
+  uint64_t reserved[5];
+};
+static_assert(sizeof(FileHeader) == 128, "table file header is 128 bytes");
+
+// Word-wise FNV-1a (64-bit offset basis and prime); a section's last partial
+// word is zero-padded.  Chunks handed in are multiples of 8 bytes except the
+// last chunk of a section.
+uint64_t fnv_words(const unsigned char* p, size_t n, uint64_t h) {
+  size_t w = n / 8;
+  for (size_t i = 0; i < w; ++i) {
+    uint64_t x;
+    memcpy(&x, p + 8 * i, 8);
+    h = (h ^ x) * 0x100000001b3ull;
+  }
+  if (n % 8) {
+    uint64_t x = 0;
+    memcpy(&x, p + 8 * w, n % 8);
+    h = (h ^ x) * 0x100000001b3ull;
+  }
+  return h;
+}
+constexpr uint64_t kFnvBasis = 0xcbf29ce484222325ull;
+
+struct Section {
+  void* dev;
+  size_t bytes;
+};
+
+int sections_of(const dft_table* t, Section out[6]) {
+  out[0] = {t->pair, (size_t)t->pair_slots * sizeof(Slot)};
+  out[1] = {t->trip, (size_t)t->trip_slots * sizeof(Slot)};
+  out[2] = {t->quad, (size_t)t->quad_slots * sizeof(Slot)};
+  out[3] = {t->prev, (size_t)t->view.V * sizeof(float)};
+  out[4] = {t->pn, (size_t)t->view.V * sizeof(float)};
+  out[5] = {t->n4c, (size_t)t->n4c_len * sizeof(float)};
+  return 6;
+}
+
+struct Staging {
+  unsigned char* buf[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  bool ok() const { return buf[0] && buf[1] && ev[0] && ev[1]; }
+  Staging() {
+    for (int i = 0; i < 2; ++i) {
+      if (cudaMallocHost(&buf[i], kChunk) != cudaSuccess) buf[i] = nullptr;
+      if (cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess) ev[i] = nullptr;
+    }
+  }
+  ~Staging() {
+    for (int i = 0; i < 2; ++i) {
+      if (buf[i]) cudaFreeHost(buf[i]);
+      if (ev[i]) cudaEventDestroy(ev[i]);
+    }
+  }
+};
+
+}  // namespace
+
+extern "C" int dft_table_save(const dft_table* t, const char* path, void* stream) {
+  if (!t || !path || !*path) return DFT_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  Staging sg;
+  if (!sg.ok()) return DFT_ERR_CUDA;
+  Section sec[6];
+  sections_of(t, sec);
+  FileHeader h;
+  memset(&h, 0, sizeof h);
+  memcpy(h.magic, kMagic, 8);
+  h.version = kFileVersion;
+  h.flags = (t->view.has_trip ? kFlagTrip : 0) | (t->view.has_quad ? kFlagQuad : 0) | (t->view.has_ctx ? kFlagCtx : 0);
+  h.V = t->view.V;
+  h.pair_slots = t->pair_slots;
+  h.trip_slots = t->trip_slots;
+  h.quad_slots = t->quad_slots;
+  h.n4c_len = t->n4c_len;
+  h.beta2 = t->view.beta2;
+  h.beta3 = t->view.beta3;
+  h.beta4 = t->view.beta4;
+  h.clip = t->view.clip;
+  // written under a temporary name and renamed, so a reader never sees a partial file
+  const std::string tmp = std::string(path) + ".partial";
+  FILE* f = fopen(tmp.c_str(), "wb");
+  if (!f) return DFT_ERR_IO;
+  int rc = DFT_OK;
+  uint64_t sum = kFnvBasis, total = 0;
+  if (fwrite(&h, sizeof h, 1, f) != 1) rc = DFT_ERR_IO;
+  // device -> pinned chunk i+1 is in flight while chunk i is hashed and written
+  for (int s = 0; s < 6 && rc == DFT_OK; ++s) {
+    const unsigned char* src = static_cast<const unsigned char*>(sec[s].dev);
+    const size_t n = sec[s].bytes;
+    const size_t nchunks = (n + kChunk - 1) / kChunk;
+    if (nchunks && (cudaMemcpyAsync(sg.buf[0], src, n < kChunk ? n : kChunk, cudaMemcpyDeviceToHost, st) !=
+                        cudaSuccess ||
+                    cudaEventRecord(sg.ev[0], st) != cudaSuccess))
+      rc = DFT_ERR_CUDA;
+    for (size_t c = 0; c < nchunks && rc == DFT_OK; ++c) {
+      const size_t off = c * kChunk, len = n - off < kChunk ? n - off : kChunk;
+      if (c + 1 < nchunks) {
+        const size_t off2 = off + kChunk, len2 = n - off2 < kChunk ? n - off2 : kChunk;
+        if (cudaMemcpyAsync(sg.buf[(c + 1) & 1], src + off2, len2, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaEventRecord(sg.ev[(c + 1) & 1], st) != cudaSuccess) {
+          rc = DFT_ERR_CUDA;
+          break;
+        }
+      }
+      if (cudaEventSynchronize(sg.ev[c & 1]) != cudaSuccess) {
+        rc = DFT_ERR_CUDA;
+        break;
+      }
+      sum = fnv_words(sg.buf[c & 1], len, sum);
+      if (fwrite(sg.buf[c & 1], 1, len, f) != len) rc = DFT_ERR_IO;
+      total += len;
+    }
+  }
+  if (rc != DFT_OK) cudaStreamSynchronize(st);  // no copy into the staging buffers may outlive them
+  h.payload_bytes = total;
+  h.checksum = sum;
+  if (rc == DFT_OK && (fseek(f, 0, SEEK_SET) != 0 || fwrite(&h, sizeof h, 1, f) != 1)) rc = DFT_ERR_IO;
+  if (fclose(f) != 0 && rc == DFT_OK) rc = DFT_ERR_IO;
+  if (rc == DFT_OK && rename(tmp.c_str(), path) != 0) rc = DFT_ERR_IO;
+  if (rc != DFT_OK) remove(tmp.c_str());
+  return rc;
+}
+
+extern "C" int dft_table_load(const char* path, dft_table** out, void* stream) {
+  if (!path || !out) return DFT_ERR_INVALID;
+  *out = nullptr;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  FILE* f = fopen(path, "rb");
+  if (!f) return DFT_ERR_IO;
+  FileHeader h;
+  const auto pow2_or_zero = [](int64_t x, bool required) {
+    if (x == 0) return !required;
+    return x >= 1024 && x <= ((int64_t)1 << 36) && (x & (x - 1)) == 0;
+  };
+  if (fread(&h, sizeof h, 1, f) != 1 || memcmp(h.magic, kMagic, 8) != 0 || h.version != kFileVersion ||
+      h.V <= 0 || h.V > ((int64_t)1 << 30) || !pow2_or_zero(h.pair_slots, true) ||
+      !pow2_or_zero(h.trip_slots, (h.flags & kFlagTrip) != 0) || !pow2_or_zero(h.quad_slots, (h.flags & kFlagQuad) != 0) ||
+      ((h.flags & kFlagTrip) == 0) != (h.trip_slots == 0) || ((h.flags & kFlagQuad) == 0) != (h.quad_slots == 0) ||
+      h.n4c_len < 0 || h.n4c_len > ((int64_t)1 << 32) || ((h.flags & kFlagQuad) == 0 && h.n4c_len != 0)) {
+    fclose(f);
+    return DFT_ERR_IO;
+  }
+  const uint64_t expect = (uint64_t)(h.pair_slots + h.trip_slots + h.quad_slots) * sizeof(Slot) +
+                          (uint64_t)(2 * h.V + h.n4c_len) * sizeof(float);
+  if (h.payload_bytes != expect) {
+    fclose(f);
+    return DFT_ERR_IO;
+  }
+  dft_table* t = new (std::nothrow) dft_table();
+  if (!t) {
+    fclose(f);
+    return DFT_ERR_CUDA;
+  }
+  cudaGetDevice(&t->device);
+  t->pair_slots = h.pair_slots;
+  t->trip_slots = h.trip_slots;
+  t->quad_slots = h.quad_slots;
+  t->n4c_len = h.n4c_len;
+  t->view.V = h.V;
+  int rc = DFT_OK;
+  const auto alloc = [&](void** p, size_t n) {
+    if (rc == DFT_OK && n && cudaMalloc(p, n) != cudaSuccess) rc = DFT_ERR_CUDA;
+  };
+  alloc(reinterpret_cast<void**>(&t->pair), (size_t)h.pair_slots * sizeof(Slot));
+  alloc(reinterpret_cast<void**>(&t->trip), (size_t)h.trip_slots * sizeof(Slot));
+  alloc(reinterpret_cast<void**>(&t->quad), (size_t)h.quad_slots * sizeof(Slot));
+  alloc(reinterpret_cast<void**>(&t->prev), (size_t)h.V * sizeof(float));
+  alloc(reinterpret_cast<void**>(&t->pn), (size_t)h.V * sizeof(float));
+  alloc(reinterpret_cast<void**>(&t->n4c), (size_t)h.n4c_len * sizeof(float));
+  Staging sg;
+  if (rc == DFT_OK && !sg.ok()) rc = DFT_ERR_CUDA;
+  Section sec[6];
+  sections_of(t, sec);
+  uint64_t sum = kFnvBasis;
+  // file -> pinned buffer c&1 waits only for the copy that last used that buffer
+  size_t c = 0;
+  bool pending[2] = {false, false};
+  for (int s = 0; s < 6 && rc == DFT_OK; ++s) {
+    unsigned char* dst = static_cast<unsigned char*>(sec[s].dev);
+    for (size_t off = 0; off < sec[s].bytes && rc == DFT_OK; off += kChunk, ++c) {
+      const size_t len = sec[s].bytes - off < kChunk ? sec[s].bytes - off : kChunk;
+      const int i = (int)(c & 1);
+      if (pending[i] && cudaEventSynchronize(sg.ev[i]) != cudaSuccess) {
+        rc = DFT_ERR_CUDA;
+        break;
+      }
+      if (fread(sg.buf[i], 1, len, f) != len) {
+        rc = DFT_ERR_IO;
+        break;
+      }
+      sum = fnv_words(sg.buf[i], len, sum);
+      if (cudaMemcpyAsync(dst + off, sg.buf[i], len, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+          cudaEventRecord(sg.ev[i], st) != cudaSuccess) {
+        rc = DFT_ERR_CUDA;
+        break;
+      }
+      pending[i] = true;
+    }
+  }
+  unsigned char extra;
+  if (rc == DFT_OK && (sum != h.checksum || fread(&extra, 1, 1, f) != 0)) rc = DFT_ERR_IO;
+  fclose(f);
+  if (cudaStreamSynchronize(st) != cudaSuccess && rc == DFT_OK) rc = DFT_ERR_CUDA;
+  if (rc != DFT_OK) {
+    free_table(t);
+    return rc;
+  }
+  set_view(t, h.V, (h.flags & kFlagTrip) != 0, (h.flags & kFlagQuad) != 0, (h.flags & kFlagCtx) != 0, h.beta2,
+           h.beta3, h.beta4, h.clip);
+  *out = t;
+  return DFT_OK;
+}
 
 // ------------------------------------------------------------ lookups ----
 

@@ -79,7 +79,7 @@ class DraftTreeCycle:
         p = self.pool
         self.pool_out = torch.as_strided(p, (Ls, B, 1, c.Hv, D, D),
                                          (p.stride(0), p.stride(1), 0, p.stride(2), p.stride(3), p.stride(4)))
-        self.launches_per_step = 3 + Ls + 1 + 1
+        self.launches_per_step = 3 + Ls + 1 + 1 + 1
 
     # -- stages --------------------------------------------------------------
     def build(self, logits, root, pre1):
@@ -107,10 +107,15 @@ class DraftTreeCycle:
         K.accept_greedy(self.tree["tokens"], self.tree["nxt"], self.tree["sib"], target, self.cfg.P,
                         status=self.status, out=(self.path, self.accept_len, self.last, self.bonus))
 
-    def commit(self):
+    def commit(self, x=None):
+        """Closed-form state commit of every layer; with the cycle's pre-conv
+        inputs x [L, B, N, C], also the conv-window commit (each layer's conv
+        state takes the last accepted node's window)."""
         c = self.cfg
         K.gdn_commit(self.pool, self.pool_out, self.aux_k, self.aux_vn, self.aux_g, self.tree["anc"], self.path,
                      self.last.view(-1, 1), c.Hk, c.Hv, aux_k_per_v=False, status=self.status)
+        if x is not None:
+            K.conv_commit(x, self.conv_state, self.tree["cidx"], self.last, status=self.status)
 
     def step(self, logits, root, pre1, x, a, b, target_fn):
         """One cycle.  x [L, B, N, C], a / b [L, B, N, Hv]; target_fn(tree) ->
@@ -119,4 +124,4 @@ class DraftTreeCycle:
         for l in range(self.cfg.layers):
             self.verify_layer(l, x[l], a[l], b[l])
         self.accept(target_fn(self.tree))
-        self.commit()
+        self.commit(x)

@@ -7,7 +7,9 @@ is captured once into a CUDA graph; `__call__` copies the inputs into the
 static buffers and replays it, like the reference.
 
 Environment, as in the reference: FC1_TREE_N (default 32), FC1_CHAIN_FIRST,
-FC1_NGRAM_PATH (npz table; `ng=` passes an already loaded NGramGPU).
+FC1_NGRAM_PATH (npz table or cached table file; `ng=` passes an already
+loaded NGramGPU).  Added here: FC1_NGRAM_CACHE, a cached-table file that is
+loaded instead of the npz when intact and written after a build otherwise.
 """
 from __future__ import annotations
 
@@ -35,7 +37,8 @@ class Builder:
         self.pre1 = torch.zeros_like(self.root)
         if ngram:
             self.ng = ng if ng is not None else NGramGPU(
-                os.environ.get("FC1_NGRAM_PATH", "data/ngram_counts.npz"), dev, beta3=60.0)
+                os.environ.get("FC1_NGRAM_PATH", "data/ngram_counts.npz"), dev, beta3=60.0,
+                cache=os.environ.get("FC1_NGRAM_CACHE") or None)
         else:
             self.ng = None
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)

@@ -7,6 +7,7 @@ batched C ABI: requests first.
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import torch
 
@@ -44,6 +45,41 @@ class Table:
         self.V = int(arrays["V"])
         self.device = dev
         self.betas = (beta2, beta3, beta4, clip)
+
+    @classmethod
+    def load(cls, path, device=None, params=None):
+        """Table from a cached file written by `save` (no npz parse, no hash build).
+        `params` = (beta2, beta3, beta4, clip) overrides the saved parameters."""
+        lib = L.lib()
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        h = C.c_void_p()
+        with torch.cuda.device(dev):
+            L.check(lib.dft_table_load(os.fsencode(path), C.byref(h), L.stream_handle()), "dft_table_load")
+        self = cls.__new__(cls)
+        self.handle, self.device = h, dev
+        self.V = self.info()["V"]
+        self.betas = None
+        if params is not None:
+            self.set_params(*params)
+        return self
+
+    def save(self, path):
+        """Write the built tables to `path` (see dft_table_save)."""
+        with torch.cuda.device(self.device):
+            L.check(L.load().dft_table_save(self.handle, os.fsencode(path), L.stream_handle()), "dft_table_save")
+
+    def set_params(self, beta2, beta3, beta4, clip):
+        L.check(L.load().dft_table_set_params(self.handle, beta2, beta3, beta4, clip), "dft_table_set_params")
+        self.betas = (beta2, beta3, beta4, clip)
+
+    def marginals(self):
+        """(prev [V], pn [V]) fp32 device copies of the table's marginals."""
+        prev = torch.empty(self.V, dtype=torch.float32, device=self.device)
+        pn = torch.empty_like(prev)
+        with torch.cuda.device(self.device):
+            L.check(L.load().dft_table_copy_marginals(self.handle, prev.data_ptr(), pn.data_ptr(),
+                                                      L.stream_handle()), "dft_table_copy_marginals")
+        return prev, pn
 
     def info(self):
         v = [C.c_int64() for _ in range(5)]
@@ -252,6 +288,32 @@ def tree_conv(x, conv_state, weight, bias, cidx, state_slots=None, y=None, iw=No
     L.check(lib.dft_tree_conv(C.byref(a), _status_ptr(status), L.stream_handle()), "dft_tree_conv")
     del keep
     return y
+
+
+def conv_commit(x, conv_state, cidx, last, slots=None, status=None):
+    """Conv-window commit: conv_state [.., slots, C, 3] of each request takes the
+    window (taps 1..3) of its last accepted node `last` [B] (< 0: unchanged).
+    x [B, N, C] or [L, B, N, C] pre-conv inputs (channel stride 1); conv_state
+    [slots, C, 3] or [L, slots, C, 3]; cidx [B, N, 4].  In place."""
+    lib = L.lib()
+    if x.dim() == 3:
+        x = x.unsqueeze(0)
+        conv_state = conv_state.unsqueeze(0)
+    Ln, B, N, Cn = x.shape
+    assert x.stride(3) == 1 and conv_state.shape[0] == Ln
+    assert conv_state.shape[2:] == (Cn, 3) and cidx.numel() == B * N * 4 and last.numel() == B
+    assert slots is not None or conv_state.shape[1] >= B
+    cidx = cidx.reshape(B, N, 4).to(torch.int64).contiguous()
+    last = last.reshape(B).to(torch.int64).contiguous()
+    slots = None if slots is None else slots.reshape(B).to(torch.int64).contiguous()
+    a = L.ConvCommitArgs(L=Ln, B=B, N=N, C=Cn, x=x.data_ptr(), x_dtype=L.dtype_code(x), x_sl=x.stride(0),
+                         x_sb=x.stride(1), x_sn=x.stride(2), conv_state=conv_state.data_ptr(),
+                         cs_dtype=L.dtype_code(conv_state), cs_sl=conv_state.stride(0), cs_ss=conv_state.stride(1),
+                         cs_sc=conv_state.stride(2), cs_st=conv_state.stride(3), slots=L.ptr(slots),
+                         cidx=cidx.data_ptr(), last=last.data_ptr())
+    keep = (cidx, last, slots)
+    L.check(lib.dft_conv_commit(C.byref(a), _status_ptr(status), L.stream_handle()), "dft_conv_commit")
+    del keep
 
 
 # -------------------------------------------------------- GDN tree verify --

@@ -6,9 +6,12 @@ clip) and the same p2 / p3 / p4 / pmi methods over broadcastable id tensors.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import torch
 
+from . import _lib as L
 from . import kernels as K
 
 
@@ -39,23 +42,63 @@ def load_npz_arrays(path_or_arrays) -> dict:
     return out
 
 
-class NGramGPU:
-    """Drop-in for dforktree.ngram_gpu.NGramGPU."""
+TABLE_MAGIC = b"DFTTABLE"
 
-    def __init__(self, path, dev, beta2=20.0, beta3=20.0, beta4=20.0, clip=10.0, max_load=0.35):
-        arrays = load_npz_arrays(path)
-        self.V = int(arrays["V"])
+
+def is_cached_table(path) -> bool:
+    """True when `path` is a file written by `NGramGPU.save` / `dft_table_save`."""
+    if isinstance(path, dict) or not isinstance(path, (str, bytes, os.PathLike)):
+        return False
+    try:
+        with open(path, "rb") as f:
+            return f.read(8) == TABLE_MAGIC
+    except OSError:
+        return False
+
+
+class NGramGPU:
+    """Drop-in for dforktree.ngram_gpu.NGramGPU.
+
+    `path` is the reference's npz (or a dict of its arrays) or a cached table
+    file.  With `cache=<file>`, an intact cached table there is loaded instead
+    of the npz; a missing or damaged one is rebuilt from the npz and written
+    back.  Either way the smoothing parameters are the ones passed here.
+    """
+
+    def __init__(self, path, dev, beta2=20.0, beta3=20.0, beta4=20.0, clip=10.0, max_load=0.35, cache=None):
         self.beta2, self.beta3, self.beta4, self.clip = beta2, beta3, beta4, clip
         dev = torch.device(dev)
         if dev.type != "cuda":
             raise RuntimeError("NGramGPU needs a CUDA device; there is no CPU path")
         self.device = dev
-        self.pn = torch.from_numpy(arrays["pn"]).to(dev)
-        self.prev = torch.from_numpy(np.asarray(arrays["prev"]).astype(np.float32)).to(dev)
-        self.has4 = "keys4" in arrays
+        params = (beta2, beta3, beta4, clip)
+        self.table = None
         with torch.cuda.device(dev):
-            self.table = K.Table(arrays, beta2, beta3, beta4, clip, max_load, device=dev)
+            for src in ([path] if is_cached_table(path) else []) + ([cache] if cache is not None else []):
+                if src is not None and os.path.exists(src):
+                    try:
+                        self.table = K.Table.load(src, device=dev, params=params)
+                        break
+                    except L.DFTError as e:
+                        if e.status != L.DFT_ERR_IO or src is path:
+                            raise
+            if self.table is not None:
+                self.prev, self.pn = self.table.marginals()
+                self.has4 = self.table.info()["quad_slots"] > 0
+            else:
+                arrays = load_npz_arrays(path)
+                self.pn = torch.from_numpy(arrays["pn"]).to(dev)
+                self.prev = torch.from_numpy(np.asarray(arrays["prev"]).astype(np.float32)).to(dev)
+                self.has4 = "keys4" in arrays
+                self.table = K.Table(arrays, beta2, beta3, beta4, clip, max_load, device=dev)
+                if cache is not None:
+                    self.table.save(cache)
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.V = self.table.V
+
+    def save(self, path):
+        """Write this table as a cached table file (loads with NGramGPU(path, dev))."""
+        self.table.save(path)
 
     def _t(self, x):
         if x is None:

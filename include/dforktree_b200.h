@@ -37,7 +37,8 @@ enum {
   DFT_ERR_CUDA = 3,         /* CUDA runtime error (launch, allocation)     */
   DFT_ERR_TABLE = 4,        /* n-gram keys unsorted, negative or too many  */
   DFT_ERR_NO_DEVICE = 5,    /* no sm_100 device current                    */
-  DFT_ERR_CAPACITY = 6      /* larger than a fixed-size static scratch     */
+  DFT_ERR_CAPACITY = 6,     /* larger than a fixed-size static scratch     */
+  DFT_ERR_IO = 7            /* table file missing, unwritable or damaged    */
 };
 enum {
   DFT_DEV_BAD_TOKEN = 1,    /* token id outside [-V, V)                    */
@@ -50,7 +51,7 @@ typedef enum { DFT_F32 = 0, DFT_BF16 = 1, DFT_F16 = 2 } dft_dtype;
 DFT_API const char* dft_status_string(int status);
 DFT_API int dft_version(void);
 
-/* ------------------------------------------------- n-gram table (A1-A3) -- */
+/* ------------------------------------------------------- n-gram table -- */
 /* Replaces NGramGPU.__init__ (ngram_gpu.py:8-26): the sorted-array npz table
  * becomes open-addressed hash tables in HBM with 16-byte slots:
  *   pair slot  {key u*V+v, bigram count n_uv, trigram-context count n3c(u,v)}
@@ -79,6 +80,23 @@ DFT_API int dft_table_destroy(dft_table* table);
 DFT_API int dft_table_info(const dft_table* table, int64_t* V, int64_t* pair_slots, int64_t* trip_slots,
                    int64_t* quad_slots, int64_t* bytes);
 
+/* Smoothing parameters of a table (e.g. after dft_table_load). */
+DFT_API int dft_table_set_params(dft_table* table, float beta2, float beta3, float beta4, float clip);
+/* Copy the table's prev[V] and pn[V] (fp32) to prev / pn (device or host;
+ * either may be NULL), stream-ordered. */
+DFT_API int dft_table_copy_marginals(const dft_table* table, float* prev, float* pn, void* stream);
+
+/* Cached binary table.  dft_table_save writes the built hash tables (slot
+ * images, prev, pn, n4c, parameters) to `path` (via a temporary file renamed
+ * into place); dft_table_load maps such a file back onto the current device
+ * with sequential reads and host-to-device copies -- no npz parse, no key
+ * sort, no hash insert -- and the loaded slots are byte-identical to the
+ * saved ones.  A missing, truncated, foreign or damaged file (64-bit checksum
+ * over the payload) returns DFT_ERR_IO.  Both synchronise `stream`.
+ * Replaces re-reading ngram_counts.npz in NGramGPU.__init__ (ngram_gpu.py:9). */
+DFT_API int dft_table_save(const dft_table* table, const char* path, void* stream);
+DFT_API int dft_table_load(const char* path, dft_table** out, void* stream);
+
 /* Elementwise p_order / PMI over flattened, pre-broadcast id arrays.
  * Replaces NGramGPU.p2/p3/p4/pmi (ngram_gpu.py:39-70).  what: 0 = p, 1 = pmi.
  * Unused ids may be NULL (z for order<4, a for order 2). */
@@ -86,7 +104,7 @@ DFT_API int dft_ngram_eval(const dft_table* table, int order, int what, const in
                    const int64_t* b, const int64_t* c, int64_t n, float* out, int32_t* dev_status,
                    void* stream);
 
-/* ------------------------------------------------ score + build (A4-A7) -- */
+/* ------------------------------------------------------ score + build -- */
 typedef struct {
   int32_t B;            /* requests                                          */
   int32_t S;            /* drafter positions (block - 1)                     */
@@ -115,17 +133,17 @@ typedef struct {
   float* keys;          /* [B, S, W] per-step beam keys                       */
 } dft_tree_out;
 
-/* A5 alone: lp, ids = topk(log_softmax(logits), M); rest (fc1_builder.py:27-28).
+/* Scoring alone: lp, ids = topk(log_softmax(logits), M); rest (fc1_builder.py:27-28).
  * logits element (b, s, v) at b*ld_b + s*ld_s + v.  ids written as int32.  */
 DFT_API int dft_score(const dft_build_params* p, const void* logits, int32_t logits_dtype, int64_t ld_b, int64_t ld_s,
               float* lp, int32_t* ids, float* rest, void* stream);
 
-/* A3/A4: dense PMI tensor T[b, t, i, j, l] of ngram_path_fn (tree_ops.py:56-65),
+/* Dense PMI tensor T[b, t, i, j, l] of ngram_path_fn (tree_ops.py:56-65),
  * order 3, over E = [pre1; root; ids].  T is [B, S-1, M, M, M] float.       */
 DFT_API int dft_pmi_dense(const dft_table* table, const dft_build_params* p, const int32_t* ids, const int64_t* root,
                   const int64_t* pre1, float* T, int32_t* dev_status, void* stream);
 
-/* A6+A7: beam search + tree structure, one CTA per request.  With use_ngram
+/* Beam search + tree structure, one CTA per request.  With use_ngram
  * the closure is the fork-aware PMI re-anchoring over T; otherwise `logc`
  * [B, S-1, M, M] (may be NULL: the no-n-gram branch of fc1_builder.py:35-36
  * is derived from lp/rest).  c0 [B, M] may be NULL (then from lp/rest). */
@@ -177,7 +195,7 @@ DFT_API int dft_accept_greedy(int32_t B, int32_t N, int32_t P, const int64_t* to
                               const int64_t* sib, const int64_t* target, int64_t* path, int64_t* accept_len,
                               int64_t* last, int64_t* bonus, int32_t* dev_status, void* stream);
 
-/* ------------------------------------------------------- tree conv (A8) -- */
+/* ---------------------------------------------------------- tree conv -- */
 /* Replaces fc1_conv.conv (fc1_conv.py:8-27) batched.  x element (b, n, c) at
  * b*x_sb + n*x_sn + c*x_sc; conv_state (slot, c, tap) at slot*cs_ss + c*cs_sc
  * + tap*cs_st (3 taps); weight [C, 4]; bias [C] or NULL; cidx [B, N, 4];
@@ -197,7 +215,24 @@ typedef struct {
 } dft_conv_args;
 DFT_API int dft_tree_conv(const dft_conv_args* a, int32_t* dev_status, void* stream);
 
-/* --------------------------------------------- GDN tree verify (A9-A12) -- */
+/* ------------------------------------------------- conv-window commit -- */
+/* After acceptance, request b's conv state becomes the window of its last
+ * accepted node u = last[b]: taps 1..3 of u, i.e. the inputs at conv columns
+ * cidx[b, u, 1..3] (columns < 3: the old conv state, 3 + m: new token m).
+ * This is what the plugin's conv hook writes into intermediate_conv_window
+ * (fc1_conv.py:22-27) and SGLang's post-verify commit copies into the conv
+ * state (after fc1_fused.py:87).  Batched over layers; in place. */
+typedef struct {
+  int32_t L, B, N, C;
+  const void* x; int32_t x_dtype; int64_t x_sl, x_sb, x_sn;          /* pre-conv (l, b, n, c), c stride 1 */
+  void* conv_state; int32_t cs_dtype; int64_t cs_sl, cs_ss, cs_sc, cs_st;   /* (l, slot, c, tap)  */
+  const int64_t* slots;           /* [B] conv-state slot of request b; NULL: slot b */
+  const int64_t* cidx;            /* [B, N, 4] conv columns                 */
+  const int64_t* last;            /* [B] last accepted node; < 0: request unchanged */
+} dft_conv_commit_args;
+DFT_API int dft_conv_commit(const dft_conv_commit_args* a, int32_t* dev_status, void* stream);
+
+/* ---------------------------------------------------- GDN tree verify -- */
 /* Replaces tree_gdn_split (tree_kernels.py:193-208 = _tree_prepare +
  * invert32 + _tree_finish) batched.  Per request b: y (b, n, col) with
  * columns [q (Hk*Dk) | k (Hk*Dk) | v (Hv*Dv)]; a, bg (b, n, h); state pool
@@ -240,7 +275,7 @@ typedef struct {
 } dft_gdn_args;
 DFT_API int dft_gdn_tree_verify(const dft_gdn_args* a, int32_t* dev_status, void* stream);
 
-/* ----------------------------------------------- closed-form commit (A13) -- */
+/* ------------------------------------------------- closed-form commit -- */
 /* Replaces fc1_fused.snapshots (fc1_fused.py:27-49) batched over layers and
  * requests: for each end u = ends[b, e] >= 0,
  *   S_u = e^{G_u} S0 + sum_{t in path[b], t anc-or-self of u} e^{G_u-G_t} vn_t k_t^T

@@ -54,6 +54,12 @@ def test_invalid_arguments_are_rejected_on_the_host(lib):
     assert lib.dft_gdn_tree_verify(None, None, None) == 1
     assert lib.dft_gdn_commit(None, None, None) == 1
     assert lib.dft_tree_conv(None, None, None) == 1
+    assert lib.dft_conv_commit(None, None, None) == 1
+    assert lib.dft_table_save(None, b"x", None) == 1
+    assert lib.dft_table_load(None, None, None) == 1
+    assert lib.dft_table_set_params(None, 20.0, 60.0, 20.0, 10.0) == 1
+    assert lib.dft_table_copy_marginals(None, None, None, None) == 1
+    assert b"table file" in lib.dft_status_string(7)
 
 
 _PROBE = r"""
@@ -68,6 +74,8 @@ int main(void) {
   printf("dft_conv_args SIZE %zu\n", sizeof(dft_conv_args));
   printf("dft_gdn_args SIZE %zu\n", sizeof(dft_gdn_args));
   printf("dft_commit_args SIZE %zu\n", sizeof(dft_commit_args));
+  printf("dft_conv_commit_args SIZE %zu\n", sizeof(dft_conv_commit_args));
+  F(dft_conv_commit_args, cs_st) F(dft_conv_commit_args, last) F(dft_conv_commit_args, x_sn)
   F(dft_table_desc, max_load) F(dft_table_desc, n4c) F(dft_build_params, lam_p)
   F(dft_conv_args, iw_slots) F(dft_conv_args, y_dtype) F(dft_gdn_args, ag_sh) F(dft_gdn_args, pool)
   F(dft_gdn_args, aux_k_per_v) F(dft_commit_args, ends) F(dft_commit_args, aux_k_per_v) F(dft_commit_args, so_sk)
@@ -86,7 +94,8 @@ def test_ctypes_layout_matches_header(tmp_path):
         pytest.skip("gcc unavailable: " + r.stderr[:200])
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
     structs = {"dft_table_desc": L.TableDesc, "dft_build_params": L.BuildParams, "dft_tree_out": L.TreeOut,
-               "dft_conv_args": L.ConvArgs, "dft_gdn_args": L.GdnArgs, "dft_commit_args": L.CommitArgs}
+               "dft_conv_args": L.ConvArgs, "dft_gdn_args": L.GdnArgs, "dft_commit_args": L.CommitArgs,
+               "dft_conv_commit_args": L.ConvCommitArgs}
     for line in out:
         if not line:
             continue
@@ -96,3 +105,21 @@ def test_ctypes_layout_matches_header(tmp_path):
             assert ctypes.sizeof(cls) == int(val), name
         else:
             assert getattr(cls, field).offset == int(val), (name, field)
+
+
+def test_table_file_header_is_checked_before_any_device_work(lib, tmp_path):
+    # missing, empty, foreign and inconsistent headers are rejected on the host (no device needed)
+    h = ctypes.c_void_p()
+    assert lib.dft_table_load(str(tmp_path / "missing.dftt").encode(), ctypes.byref(h), None) == 7
+    cases = [b"", b"DFTTABLE" + b"\0" * 40, b"NOTATABL" + b"\0" * 120]
+    import struct
+    hdr = struct.pack("<8sII5q4fQQ5Q", b"DFTTABLE", 1, 0, 1000, 1024, 0, 0, 0, 20.0, 60.0, 20.0, 10.0,
+                      12345, 0, 0, 0, 0, 0, 0)
+    assert len(hdr) == 128
+    cases.append(hdr)                                           # payload size disagrees with the slots
+    cases.append(hdr[:8] + struct.pack("<I", 2) + hdr[12:])     # unknown version
+    for i, blob in enumerate(cases):
+        p = tmp_path / f"h{i}.dftt"
+        p.write_bytes(blob)
+        assert lib.dft_table_load(str(p).encode(), ctypes.byref(h), None) == 7, i
+        assert not h.value

@@ -138,6 +138,7 @@ def test_cycle_step_matches_oracle_chain():
     cfg = CycleConfig(B=B, S=S, V=V, N=N, layers=Ls)
     cyc = DraftTreeCycle(cfg, K.Table(load_npz_arrays(table), beta3=60.0), DEV, seed=5)
     pool0 = cyc.pool.clone()
+    cs0 = cyc.conv_state.clone()
     logits = np.stack([synth.make_logits(S, V, seed=600 + r) for r in range(B)])
     lt = torch.from_numpy(logits).to(DEV)
     root = torch.tensor([11, 22, 33, 44], device=DEV)
@@ -171,10 +172,55 @@ def test_cycle_step_matches_oracle_chain():
         assert list(path[r][: len(p)]) == p and np.all(path[r][len(p):] == -1)
         for l in range(Ls):
             xr = _np(x[l, r])
-            y, _ = OG.tree_conv(xr, _np(cyc.conv_state[l, r]), _np(cyc.conv_w[l]), None, tr["cidx"])
+            y, _ = OG.tree_conv(xr, _np(cs0[l, r]), _np(cyc.conv_w[l]), None, tr["cidx"])
             y = _np(torch.from_numpy(y).to(torch.bfloat16))      # the conv output is stored in x's dtype
             o, k, vn, G = OG.tree_gdn(y, _np(a[l, r]), _np(b[l, r]), _np(cyc.A_log[l]), _np(cyc.dt_bias[l]),
                                       _np(pool0[l]), r, tr["anc"], cfg.Hk, cfg.Hv, 128, 128)
             for h in range(cfg.Hv):
                 ref = OG.snapshot(_np(pool0[l, r, h]), k[h], vn[h], G[h], tr["anc"], path[r], p[-1])
                 assert _rel(_np(cyc.pool[l, r, h]), ref) < 1e-3, (r, l, h)
+            # conv-window commit: taps 1..3 of the last accepted node (old state columns or new inputs)
+            cols = tr["cidx"][p[-1], 1:]
+            src = [_np(cs0[l, r])[:, c] if c < 3 else xr[c - 3] for c in cols]
+            np.testing.assert_array_equal(_np(cyc.conv_state[l, r]), np.stack(src, 1))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_conv_commit_slots_skips_and_bad_index(dtype):
+    """Conv-window commit through the C ABI: per layer and request the state
+    takes taps 1..3 of node last[b] (state columns or new inputs, by cidx);
+    last < 0 leaves it untouched; slots map requests to pool rows."""
+    from dforktree_b200 import kernels as K
+    from dforktree_b200 import synth
+    Ls, B, N, C, slots_n = 3, 5, 32, 1000, 9
+    rng = np.random.default_rng(21)
+    cidx = np.stack([OB.tree_struct(synth.random_tree_parents(N, rng), 4)[2] for _ in range(B)])
+    g = torch.Generator(device=DEV)
+    g.manual_seed(4)
+    x = torch.randn(Ls, B, N, C, device=DEV, generator=g).to(dtype)
+    cs = torch.randn(Ls, slots_n, C, 3, device=DEV, generator=g).to(dtype)
+    slots = torch.tensor([7, 0, 3, 8, 5], device=DEV)
+    last = torch.tensor([0, 31, -1, 17, 5], device=DEV)
+    cs0 = _np(cs.float())
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    K.conv_commit(x, cs, torch.from_numpy(cidx).to(DEV), last, slots=slots, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    got, xs = _np(cs.float()), _np(x.float())
+    want = cs0.copy()
+    for l in range(Ls):
+        for bi in range(B):
+            u = int(last[bi])
+            if u < 0:
+                continue
+            s = int(slots[bi])
+            for j, col in enumerate(cidx[bi, u, 1:]):
+                want[l, s, :, j] = cs0[l, s, :, col] if col < 3 else xs[l, bi, col - 3]
+    np.testing.assert_array_equal(got, want)
+    # a last-node index past the tree raises BAD_INDEX and writes nothing for that request
+    cs1 = cs.clone()
+    K.conv_commit(x, cs, torch.from_numpy(cidx).to(DEV), torch.tensor([-1, -1, 40, -1, -1], device=DEV),
+                  slots=slots, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) & 4
+    assert torch.equal(cs, cs1)
