@@ -72,6 +72,15 @@ class ConvCommitArgs(C.Structure):
                 ("slots", vp), ("cidx", vp), ("last", vp)]
 
 
+class TreeAttnArgs(C.Structure):
+    _fields_ = [("B", i32), ("N", i32), ("Hq", i32), ("Hkv", i32), ("D", i32),
+                ("q", vp), ("q_sb", i64), ("q_sn", i64), ("q_sh", i64),
+                ("k_cache", vp), ("v_cache", vp), ("kv_st", i64), ("kv_sh", i64), ("n_slots", i64),
+                ("kv_indptr", vp), ("kv_indices", vp), ("anc", vp), ("anc_sb", i64),
+                ("sm_scale", f32), ("max_kv_len", i32),
+                ("o", vp), ("o_sb", i64), ("o_sn", i64), ("o_sh", i64)]
+
+
 class GdnConvArgs(C.Structure):
     _fields_ = [("x", vp), ("x_dtype", i32), ("x_sb", i64), ("x_sn", i64),
                 ("conv_state", vp), ("cs_dtype", i32), ("cs_ss", i64), ("cs_sc", i64), ("cs_st", i64),
@@ -134,6 +143,8 @@ SIGNATURES = {
     "dft_accept_greedy": (C.c_int, [i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "dft_tree_conv": (C.c_int, [C.POINTER(ConvArgs), vp, vp]),
     "dft_conv_commit": (C.c_int, [C.POINTER(ConvCommitArgs), vp, vp]),
+    "dft_tree_attn_workspace_bytes": (i64, [C.POINTER(TreeAttnArgs)]),
+    "dft_tree_attn": (C.c_int, [C.POINTER(TreeAttnArgs), vp, vp, vp]),
     "dft_gdn_tree_verify": (C.c_int, [C.POINTER(GdnArgs), vp, vp]),
     "dft_gdn_commit": (C.c_int, [C.POINTER(CommitArgs), vp, vp]),
 }

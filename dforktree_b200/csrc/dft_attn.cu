@@ -1,0 +1,525 @@
+// Tree-masked attention verify for the gated full-attention layers (sm_100a).
+//
+// Reference: the plugin verifies a 32-node draft tree through SGLang's
+// flashinfer prefill wrapper with a custom mask (fc1_branch64.py:39 builds
+// mask = [ones(n, prefix) | anc], fc1_plan.py:16-33 plans one request with
+// page size 1 and the host-known KV length).  Per request and q-head:
+//   o[n] = softmax_j( q[n] . k[j] * sm_scale  |  j < prefix or anc[n][j - prefix] ) . v[j]
+// with grouped-query heads (q-head hq reads kv-head hq / G).
+//
+// Here: one CTA per work unit (request b, kv-head h, key split s).  The G
+// q-heads of kv-head h and the N tree nodes form one 128-row query tile
+// (row = node * G + head), so one tcgen05 MMA of M = 128 serves the whole
+// group:
+//   Q   TMA (4-D tensor map, 128-byte swizzle) -> shared, once per unit
+//   K,V 64-key tiles gathered through the page table (page size 1) with
+//       16-byte cp.async into the 128B-swizzled layout, two stages, four
+//       producer warps (the paged rows rule out tiled TMA)
+//   S   = Q K^T    tcgen05 kind::f16 (bf16 in, fp32 out), M=128 N=64 K=256, TMEM
+//   P   = exp2(S * scale*log2e - m) with the tree mask, one thread per row
+//       (TMEM lane); running max rescales O in TMEM only when it grows by
+//       more than 2^8, P to shared as bf16 (K-major, swizzled)
+//   O  += P V      tcgen05 kind::f16, V as an MN-major operand, M=128 N=256 K=64
+// S is double-buffered in TMEM (O 256 columns + 2 x 64), so the S MMA of
+// tile t+1 runs while the softmax of tile t does.  Splits write (O, m, l)
+// partials that a second kernel merges; a single split writes o directly.
+// Every wait is bounded (~1 s); on timeout the CTA raises DFT_DEV_TIMEOUT,
+// drains its copies and MMAs (bounded), frees TMEM and exits.
+#include "dft_common.cuh"
+#include "dft_tc.cuh"
+
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+
+using namespace dft;
+using namespace dft::tc;
+
+namespace {
+
+constexpr int kD = 256;        // head dim (tensor-core path)
+constexpr int kRows = 128;     // query rows per unit (nodes x group)
+constexpr int kKeys = 64;      // keys per tile
+constexpr int kThreads = 288;  // warps 0-3 softmax / epilogue, 4 control + MMA, 5-8 KV producers
+constexpr int kProducers = 128;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t COL_O = 0, COL_S = 256;  // S buffer b at COL_S + 64 b
+
+constexpr uint32_t kQChunk = kRows * 128;   // 16 KB: 128 rows x 64 dims
+constexpr uint32_t kKVChunk = kKeys * 128;  // 8 KB: 64 keys x 64 dims
+constexpr uint32_t kKVTile = 4 * kKVChunk;  // 32 KB
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_KV = 64 * 1024;      // stage s: K at + 64 KB s, V at + 64 KB s + 32 KB
+constexpr uint32_t OFF_P = 192 * 1024;      // P buffer b at + 16 KB b
+constexpr uint32_t OFF_SMALL = 224 * 1024;
+constexpr uint32_t kSmallBytes = 512;
+constexpr uint32_t kSmem = OFF_SMALL + kSmallBytes + 1024;  // + alignment slack
+
+struct Small {
+  uint64_t q_full;
+  uint64_t kv_full[2], kv_empty[2];
+  uint64_t s_full[2], s_free[2];
+  uint64_t p_full[2], p_free[2];
+  uint64_t o_done, mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert(sizeof(Small) <= kSmallBytes, "small region");
+
+struct AttnParams {
+  dft_tree_attn_args a;
+  int G;          // q-heads per kv-head
+  int splits;     // key splits per (request, kv-head)
+  int tps;        // tiles per split
+  float* ws_o;    // [units][128][256] partial O (splits > 1)
+  float* ws_ml;   // [units][128][2]   partial (m, l)
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+
+__device__ __forceinline__ void set_abort(Small& sm, int32_t* status) {
+  *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+  raise_status(status, DFT_DEV_TIMEOUT);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    tree_attn_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ AttnParams P, int32_t* status) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  Small& sm = *reinterpret_cast<Small*>(smem + OFF_SMALL);
+  const volatile int* abort_flag = &sm.abort;
+  const dft_tree_attn_args& a = P.a;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int unit = blockIdx.x;
+  const int s = unit % P.splits;
+  const int h = (unit / P.splits) % a.Hkv;
+  const int b = unit / (P.splits * a.Hkv);
+  const uint32_t sbase = smem_u32(smem);
+
+  // keys of request b: kv_indices[start, start + len); the last N are the tree nodes
+  const int64_t kv_start = a.kv_indptr[b];
+  int len = (int)(a.kv_indptr[b + 1] - kv_start);
+  if (len < a.N || len > a.max_kv_len) {
+    if (tid == 0) raise_status(status, DFT_DEV_BAD_INDEX);
+    len = 0;
+  }
+  const int plen = len - a.N;
+  const int n_tiles = (len + kKeys - 1) / kKeys;
+  const int t0 = s * P.tps;
+  const int t1 = min(t0 + P.tps, n_tiles);
+  const int T = t1 > t0 ? t1 - t0 : 0;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      mbar_init(smem_u32(&sm.q_full), 1);
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(smem_u32(&sm.kv_full[i]), kProducers);
+        mbar_init(smem_u32(&sm.kv_empty[i]), 1);
+        mbar_init(smem_u32(&sm.s_full[i]), 1);
+        mbar_init(smem_u32(&sm.s_free[i]), kRows);
+        mbar_init(smem_u32(&sm.p_full[i]), kRows);
+        mbar_init(smem_u32(&sm.p_free[i]), 1);
+      }
+      mbar_init(smem_u32(&sm.o_done), 1);
+      mbar_init(smem_u32(&sm.mma_done), 1);
+      sm.abort = 0;
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    tmem_alloc(smem_u32(&sm.tmem_base), kTmemCols);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 4) {
+    // ------------------------------------------------ control: Q load + MMAs
+    if (lane == 0 && T > 0) {
+      const uint64_t pol = l2_evict_first();
+      const uint32_t qf = smem_u32(&sm.q_full);
+      mbar_expect_tx(qf, 4 * kQChunk);
+      for (int c = 0; c < 4; ++c) tma_load_4d(sbase + OFF_Q + c * kQChunk, &q_map, 64 * c, h * P.G, 0, b, qf, pol);
+      bool ok = mbar_wait_or_abort(qf, 0, abort_flag);
+      const uint32_t id_s = idesc_bf16(128, kKeys, false), id_o = idesc_bf16(128, kD, true);
+      for (int t = 0; ok && t <= T; ++t) {
+        if (t < T) {
+          const int st = t & 1;
+          ok = mbar_wait_or_abort(smem_u32(&sm.kv_full[st]), (t >> 1) & 1, abort_flag);
+          if (ok && t >= 2) ok = mbar_wait_or_abort(smem_u32(&sm.s_free[st]), ((t >> 1) - 1) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          fence_async_smem();  // cp.async (generic proxy) writes -> tensor-core reads
+          const uint32_t kb = sbase + OFF_KV + st * 2 * kKVTile;
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const uint64_t ad = sw128_desc(sbase + OFF_Q + (k >> 2) * kQChunk + (k & 3) * 32);
+            const uint64_t bd = sw128_desc(kb + (k >> 2) * kKVChunk + (k & 3) * 32);
+            mma_bf16(tmem + COL_S + 64 * st, ad, bd, id_s, k > 0);
+          }
+          mma_commit(smem_u32(&sm.s_full[st]));
+        }
+        if (t >= 1) {
+          const int u = t - 1, pb = u & 1;
+          ok = mbar_wait_or_abort(smem_u32(&sm.p_full[pb]), (u >> 1) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t vb = sbase + OFF_KV + (u & 1) * 2 * kKVTile + kKVTile;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = sw128_desc(sbase + OFF_P + pb * kQChunk + k * 32);
+            // V [keys x dims] is MN-major: 64-dim chunks 8 KB apart, 8-key groups 1 KB apart
+            const uint64_t bd = sw128_desc(vb + k * 16 * 128, kKVChunk, 1024);
+            mma_bf16(tmem + COL_O, ad, bd, id_o, (u > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(smem_u32(&sm.kv_empty[u & 1]));
+          mma_commit(smem_u32(&sm.p_free[pb]));
+          mma_commit(smem_u32(&sm.o_done));
+        }
+      }
+      if (!ok && !*abort_flag) set_abort(sm, status);
+      // every MMA issued above has retired before TMEM is freed
+      mma_commit(smem_u32(&sm.mma_done));
+      if (!mbar_wait(smem_u32(&sm.mma_done), 0)) raise_status(status, DFT_DEV_TIMEOUT);
+    }
+    __syncwarp();
+  } else if (warp >= 5) {
+    // ------------------------------------------- producers: paged K/V gather
+    const int p = tid - 160, pw = p >> 5;
+    const uint64_t pol = l2_evict_first();
+    const unsigned char* kc = static_cast<const unsigned char*>(a.k_cache);
+    const unsigned char* vc = static_cast<const unsigned char*>(a.v_cache);
+    const int64_t head_off = (int64_t)h * a.kv_sh * 2 + (int64_t)lane * 16;
+    const uint32_t dst_lane = (uint32_t)(lane >> 3) * kKVChunk;
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      const int st = t & 1;
+      if (t >= 2) {
+        ok = mbar_wait_or_abort(smem_u32(&sm.kv_empty[st]), ((t >> 1) - 1) & 1, abort_flag);
+        if (!ok) break;
+      }
+      const uint32_t kb = sbase + OFF_KV + st * 2 * kKVTile, vb = kb + kKVTile;
+      const int j0 = (t0 + t) * kKeys;
+#pragma unroll 4
+      for (int kk = 0; kk < kKeys / 4; ++kk) {
+        const int r = kk * 4 + pw;
+        const int j = j0 + r;
+        bool valid = j < len;
+        int64_t slot = valid ? (int64_t)a.kv_indices[kv_start + j] : 0;
+        if (valid && (slot < 0 || slot >= a.n_slots)) {
+          if (lane == 0) raise_status(status, DFT_DEV_BAD_INDEX);
+          valid = false;
+          slot = 0;
+        }
+        const int64_t off = slot * a.kv_st * 2 + head_off;
+        const uint32_t dst = dst_lane + (uint32_t)r * 128 + ((((uint32_t)lane & 7) ^ ((uint32_t)r & 7)) << 4);
+        cp_async16(kb + dst, valid ? kc + off : kc, valid ? 16u : 0u, pol);
+        cp_async16(vb + dst, valid ? vc + off : vc, valid ? 16u : 0u, pol);
+      }
+      cp_async_arrive_noinc(smem_u32(&sm.kv_full[st]));
+    }
+    cp_async_wait_all();
+    if (!ok && !*abort_flag) set_abort(sm, status);
+  } else {
+    // ------------------------------------- softmax / epilogue: one row each
+    const int r = tid;  // TMEM lane r
+    const int n = r / P.G, g = r % P.G;
+    const bool row_ok = n < a.N;
+    uint64_t mask = 0;  // bit m: tree node m is n or an ancestor of n
+    if (row_ok) {
+      const float* arow = a.anc + (int64_t)b * a.anc_sb + (int64_t)n * a.N;
+      for (int m = 0; m < a.N; ++m)
+        if (__ldg(arow + m) > 0.5f) mask |= 1ull << m;
+    }
+    const float sc = a.sm_scale * 1.4426950408889634f;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // tcgen05.ld / st are warp-collective: every branch around them is
+    // warp-uniform (waits are reduced over the warp, the rescale decision too)
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      const int sb = t & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(smem_u32(&sm.s_full[sb]), (t >> 1) & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      float x[64];
+      {
+        float v[32];
+        tmem_ld32(tmem + lane_base + COL_S + 64 * sb, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[i] = v[i];
+        tmem_ld32(tmem + lane_base + COL_S + 64 * sb + 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[32 + i] = v[i];
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&sm.s_free[sb]));
+      const int j0 = (t0 + t) * kKeys;
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const int j = j0 + i;
+        float y = x[i] * sc;
+        if (j >= len) y = -INFINITY;
+        else if (j >= plen && !((mask >> (j - plen)) & 1ull)) y = -INFINITY;
+        x[i] = y;
+        tmax = fmaxf(tmax, y);
+      }
+      // a row moves its reference max only when the tile max exceeds it by
+      // more than 8 (P <= 2^8 otherwise); O then scales by 2^(old - new)
+      const bool grow = tmax > m_used + 8.f;
+      if (__any_sync(0xffffffffu, grow)) {
+        const float m_new = grow ? tmax : m_used;
+        if (t > 0) {
+          // O holds P V of tiles < t: wait for the last of them, then rescale
+          ok = __all_sync(0xffffffffu, mbar_wait_or_abort(smem_u32(&sm.o_done), (t - 1) & 1, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+          const float alpha = grow ? ex2(m_used - m_new) : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < kD / 32; ++c) {
+            float v[32];
+            tmem_ld32(tmem + lane_base + COL_O + 32 * c, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= alpha;
+            tmem_st32(tmem + lane_base + COL_O + 32 * c, v);
+          }
+          l *= alpha;
+        }
+        m_used = m_new;
+      }
+      uint32_t pk[32];
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = x[2 * i] == -INFINITY ? 0.f : ex2(x[2 * i] - m_used);
+        const float p1 = x[2 * i + 1] == -INFINITY ? 0.f : ex2(x[2 * i + 1] - m_used);
+        pk[i] = pack_bf16(p0, p1);
+        sum += bf16_lo(pk[i]) + bf16_hi(pk[i]);
+      }
+      l += sum;
+      const int pb = t & 1;
+      if (t >= 2) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait_or_abort(smem_u32(&sm.p_free[pb]), ((t >> 1) - 1) & 1, abort_flag));
+        if (!ok) break;
+      }
+      unsigned char* prow = smem + OFF_P + pb * kQChunk + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      fence_async_smem();  // generic stores -> tensor-core reads
+      tc_fence_before();
+      mbar_arrive(smem_u32(&sm.p_full[pb]));
+    }
+    // the last P V has retired once every MMA has (o_done's parity cannot tell
+    // its final phase from the one before: the last S MMA precedes two P V)
+    if (ok && T > 0) ok = __all_sync(0xffffffffu, mbar_wait_or_abort(smem_u32(&sm.mma_done), 0, abort_flag));
+    if (!ok && !*abort_flag) set_abort(sm, status);
+    tc_fence_after();
+    const bool have = ok && T > 0;  // warp-uniform
+    if (P.splits == 1) {
+      if (have) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        unsigned char* orow = static_cast<unsigned char*>(a.o) +
+                              ((int64_t)b * a.o_sb + (int64_t)n * a.o_sn + (int64_t)(h * P.G + g) * a.o_sh) * 2;
+#pragma unroll 1
+        for (int c = 0; c < kD / 32; ++c) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + COL_O + 32 * c, v);
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              dst[q] = make_uint4(pack_bf16(v[8 * q] * inv, v[8 * q + 1] * inv),
+                                  pack_bf16(v[8 * q + 2] * inv, v[8 * q + 3] * inv),
+                                  pack_bf16(v[8 * q + 4] * inv, v[8 * q + 5] * inv),
+                                  pack_bf16(v[8 * q + 6] * inv, v[8 * q + 7] * inv));
+          }
+        }
+      }
+    } else {
+      const int64_t prow = (int64_t)unit * kRows + r;
+      float4* dst = reinterpret_cast<float4*>(P.ws_o + prow * kD);
+      const bool mine = have && l > 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kD / 32; ++c) {
+        float v[32];
+        if (have) tmem_ld32(tmem + lane_base + COL_O + 32 * c, v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          dst[8 * c + q] = mine ? make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3])
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      P.ws_ml[2 * prow] = mine ? m_used : -INFINITY;
+      P.ws_ml[2 * prow + 1] = mine ? l : 0.f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Merge the split partials of one output row (request b, node n, q-head hq):
+// o = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.  64 threads x 4 dims.
+__global__ void __launch_bounds__(64) tree_attn_combine(const __grid_constant__ AttnParams P) {
+  const dft_tree_attn_args& a = P.a;
+  const int nh = blockIdx.x, b = blockIdx.y;
+  const int n = nh / a.Hq, hq = nh % a.Hq;
+  const int h = hq / P.G, g = hq % P.G;
+  const int r = n * P.G + g;
+  const int64_t u0 = ((int64_t)b * a.Hkv + h) * P.splits;
+  float M = -INFINITY;
+  for (int s = 0; s < P.splits; ++s) M = fmaxf(M, P.ws_ml[2 * ((u0 + s) * kRows + r)]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float L = 0.f;
+  for (int s = 0; s < P.splits; ++s) {
+    const int64_t prow = (u0 + s) * kRows + r;
+    const float ls = P.ws_ml[2 * prow + 1];
+    if (!(ls > 0.f)) continue;
+    const float w = ex2(P.ws_ml[2 * prow] - M);
+    const float4 v = reinterpret_cast<const float4*>(P.ws_o + prow * kD)[threadIdx.x];
+    acc.x += w * v.x;
+    acc.y += w * v.y;
+    acc.z += w * v.z;
+    acc.w += w * v.w;
+    L += w * ls;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  unsigned char* orow = static_cast<unsigned char*>(a.o) +
+                        ((int64_t)b * a.o_sb + (int64_t)n * a.o_sn + (int64_t)hq * a.o_sh) * 2;
+  reinterpret_cast<uint2*>(orow)[threadIdx.x] = make_uint2(pack_bf16(acc.x * inv, acc.y * inv), pack_bf16(acc.z * inv, acc.w * inv));
+}
+
+// ------------------------------------------------------------------ host --
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+inline bool al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+int check_args(const dft_tree_attn_args* a) {
+  if (!a || !a->q || !a->k_cache || !a->v_cache || !a->kv_indptr || !a->kv_indices || !a->anc || !a->o)
+    return DFT_ERR_INVALID;
+  if (a->B <= 0 || a->N <= 0 || a->Hq <= 0 || a->Hkv <= 0 || a->Hq % a->Hkv || a->max_kv_len < a->N ||
+      a->n_slots <= 0 || a->B > 65535)
+    return DFT_ERR_INVALID;
+  const int G = a->Hq / a->Hkv;
+  if (a->D != kD || (G != 1 && G != 2 && G != 4 && G != 8) || a->N * G > kRows || a->N > 64)
+    return DFT_ERR_UNSUPPORTED;
+  if (!al16(a->q) || !al16(a->k_cache) || !al16(a->v_cache) || !al16(a->o)) return DFT_ERR_UNSUPPORTED;
+  if ((a->q_sh * 2) % 16 || (a->q_sn * 2) % 16 || (a->q_sb * 2) % 16 || (a->kv_st * 2) % 16 ||
+      (a->kv_sh * 2) % 16 || (a->o_sh * 2) % 16 || (a->o_sn * 2) % 16 || (a->o_sb * 2) % 16)
+    return DFT_ERR_UNSUPPORTED;
+  if (a->q_sh < kD || a->q_sn <= 0 || a->q_sb <= 0) return DFT_ERR_UNSUPPORTED;
+  return DFT_OK;
+}
+
+// Key splits per (request, kv-head): the fewest that fill the SMs' waves to
+// >= 90 % (partials cost 1 KB per row and split, kept in L2 by the merge).
+void plan(const dft_tree_attn_args* a, int* splits, int* tps) {
+  const int tiles = (a->max_kv_len + kKeys - 1) / kKeys;
+  const int64_t pairs = (int64_t)a->B * a->Hkv;
+  const int sms = sm_count();
+  int best = 1;
+  double best_eff = 0.0;
+  for (int sp = 1; sp <= 8 && sp <= tiles; ++sp) {
+    const int64_t units = pairs * sp;
+    const int64_t waves = (units + sms - 1) / sms;
+    const double eff = (double)units / (double)(waves * sms);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = sp;
+    }
+    if (eff >= 0.9) break;
+  }
+  *splits = best;
+  *tps = (tiles + best - 1) / best;
+}
+
+}  // namespace
+
+extern "C" int64_t dft_tree_attn_workspace_bytes(const dft_tree_attn_args* a) {
+  if (check_args(a)) return -1;
+  int splits, tps;
+  plan(a, &splits, &tps);
+  if (splits == 1) return 0;
+  const int64_t units = (int64_t)a->B * a->Hkv * splits;
+  return units * kRows * (kD + 2) * (int64_t)sizeof(float);
+}
+
+extern "C" int dft_tree_attn(const dft_tree_attn_args* a, void* workspace, int32_t* dev_status, void* stream) {
+  const int rc = check_args(a);
+  if (rc) return rc;
+  if (!encode_fn()) return DFT_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  AttnParams P;
+  memset(&P, 0, sizeof(P));
+  P.a = *a;
+  P.G = a->Hq / a->Hkv;
+  plan(a, &P.splits, &P.tps);
+  const int64_t units = (int64_t)a->B * a->Hkv * P.splits;
+  if (P.splits > 1) {
+    if (!workspace || !al16(workspace)) return DFT_ERR_INVALID;
+    P.ws_o = static_cast<float*>(workspace);
+    P.ws_ml = P.ws_o + units * kRows * kD;
+  }
+  if (units > 0x7FFFFFFF) return DFT_ERR_UNSUPPORTED;
+  CUtensorMap q_map;
+  {
+    // q as [B][N][Hq][D]: box = 64 dims x G heads x (128 / G) nodes; nodes >= N read as zeros
+    const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)a->Hq, (cuuint64_t)a->N, (cuuint64_t)a->B};
+    const cuuint64_t strides[3] = {(cuuint64_t)(a->q_sh * 2), (cuuint64_t)(a->q_sn * 2), (cuuint64_t)(a->q_sb * 2)};
+    const cuuint32_t box[4] = {64, (cuuint32_t)P.G, (cuuint32_t)(kRows / P.G), 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (encode_fn()(&q_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a->q), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return DFT_ERR_UNSUPPORTED;
+  }
+  if (cudaFuncSetAttribute(tree_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) != cudaSuccess)
+    return DFT_ERR_CUDA;
+  tree_attn_kernel<<<(unsigned)units, kThreads, kSmem, st>>>(q_map, P, dev_status);
+  DFT_LAUNCH_CHECK();
+  if (P.splits > 1) {
+    dim3 grid((unsigned)(a->N * a->Hq), (unsigned)a->B);
+    tree_attn_combine<<<grid, 64, 0, st>>>(P);
+    DFT_LAUNCH_CHECK();
+  }
+  return DFT_OK;
+}

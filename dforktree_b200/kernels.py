@@ -434,3 +434,51 @@ def gdn_commit(state_in, state_out, aux_k, aux_vn, aux_g, anc, path, ends, Hk, H
     L.check(lib.dft_gdn_commit(C.byref(args), _status_ptr(status), L.stream_handle()), "dft_gdn_commit")
     del keep
     return state_out
+
+
+# ----------------------------------------------------- tree-masked attention --
+def tree_attn_args(q, k_cache, v_cache, kv_indptr, kv_indices, anc, max_kv_len, sm_scale=None, o=None):
+    """(ctypes args, o, kept tensors) for dft_tree_attn; shapes as tree_attention."""
+    B, N, Hq, D = q.shape
+    slots, Hkv, Dk = k_cache.shape
+    if v_cache.shape != k_cache.shape or v_cache.stride() != k_cache.stride() or Dk != D:
+        raise L.DFTError("tree_attention: k_cache / v_cache must both be [slots, Hkv, D] with equal strides")
+    if q.stride(3) != 1 or k_cache.stride(2) != 1:
+        raise L.DFTError("tree_attention: the head dim must be contiguous")
+    if o is None:
+        o = torch.empty(B, N, Hq, D, dtype=q.dtype, device=q.device)
+    kv_indptr = kv_indptr.to(torch.int32).contiguous()
+    kv_indices = kv_indices.to(torch.int32).contiguous()
+    anc = anc.reshape(B, N, N).to(torch.float32).contiguous()
+    a = L.TreeAttnArgs(B=B, N=N, Hq=Hq, Hkv=Hkv, D=D, q=q.data_ptr(), q_sb=q.stride(0), q_sn=q.stride(1),
+                       q_sh=q.stride(2), k_cache=k_cache.data_ptr(), v_cache=v_cache.data_ptr(),
+                       kv_st=k_cache.stride(0), kv_sh=k_cache.stride(1), n_slots=slots,
+                       kv_indptr=kv_indptr.data_ptr(), kv_indices=kv_indices.data_ptr(), anc=anc.data_ptr(),
+                       anc_sb=N * N, sm_scale=float(D ** -0.5 if sm_scale is None else sm_scale),
+                       max_kv_len=int(max_kv_len), o=o.data_ptr(), o_sb=o.stride(0), o_sn=o.stride(1),
+                       o_sh=o.stride(2))
+    return a, o, (kv_indptr, kv_indices, anc)
+
+
+def tree_attention(q, k_cache, v_cache, kv_indptr, kv_indices, anc, max_kv_len=None, sm_scale=None, o=None,
+                   workspace=None, status=None):
+    """Tree-masked attention verify: q [B, N, Hq, D] bf16; k_cache / v_cache
+    [slots, Hkv, D] bf16 (page size 1); request b's keys are
+    kv_indices[kv_indptr[b]:kv_indptr[b+1]] (prefix first, then the N tree
+    nodes); anc [B, N, N] ancestor-or-self.  max_kv_len: host-known bound on
+    the per-request key count (read from kv_indptr, with a sync, if None).
+    Returns o [B, N, Hq, D]."""
+    lib = L.lib()
+    if max_kv_len is None:
+        ptr = kv_indptr.to(torch.int64)
+        max_kv_len = int((ptr[1:] - ptr[:-1]).max().item())
+    a, o, keep = tree_attn_args(q, k_cache, v_cache, kv_indptr, kv_indices, anc, max_kv_len, sm_scale, o)
+    need = lib.dft_tree_attn_workspace_bytes(C.byref(a))
+    if need < 0:
+        raise L.DFTError("tree_attention: shape outside the tensor-core path (D = 256, G in {1,2,4,8}, N*G <= 128)")
+    if need > 0 and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    L.check(lib.dft_tree_attn(C.byref(a), None if need == 0 else workspace.data_ptr(), _status_ptr(status),
+                              L.stream_handle()), "dft_tree_attn")
+    del keep
+    return o

@@ -297,6 +297,38 @@ typedef struct {
 } dft_commit_args;
 DFT_API int dft_gdn_commit(const dft_commit_args* a, int32_t* dev_status, void* stream);
 
+/* ------------------------------------------ tree-masked attention verify -- */
+/* Replaces the flashinfer paged prefill the plugin plans for the gated
+ * full-attention layers (fc1_plan.py:16-33, mask from fc1_branch64.py:39):
+ * per request b, tree node n and q-head hq,
+ *   o[b,n,hq] = softmax_j(q[b,n,hq] . k[j,hq/G] * sm_scale) . v[j,hq/G]
+ * over the request's keys j = kv_indices[kv_indptr[b] .. kv_indptr[b+1]),
+ * page size 1; the last N of them are the tree nodes in node order, and a
+ * tree key m is visible to node n iff anc[b, n, m] > 0.5 (every prefix key
+ * is visible).  bf16 q / caches / o, fp32 accumulation, P rounded to bf16
+ * for the second MMA (as the reference's fa2 kernel does).  Tensor-core path:
+ * D = 256, G = Hq / Hkv in {1,2,4,8}, N * G <= 128, N <= 64, 16-byte aligned
+ * rows and strides; other shapes return DFT_ERR_UNSUPPORTED.
+ * max_kv_len is the host-known bound on any request's key count (the plan's
+ * HOST_KV_LEN); it sizes the key splits.  Splits > 1 need the workspace
+ * (dft_tree_attn_workspace_bytes; 0 means none).  Keys outside
+ * [0, n_slots) and lengths outside [N, max_kv_len] set DFT_DEV_BAD_INDEX. */
+typedef struct {
+  int32_t B, N, Hq, Hkv, D;
+  const void* q; int64_t q_sb, q_sn, q_sh;      /* [B, N, Hq, D] bf16      */
+  const void* k_cache; const void* v_cache;     /* [slots, Hkv, D] bf16    */
+  int64_t kv_st, kv_sh;                         /* slot / head strides     */
+  int64_t n_slots;
+  const int32_t* kv_indptr;                     /* [B + 1]                 */
+  const int32_t* kv_indices;                    /* token slots             */
+  const float* anc; int64_t anc_sb;             /* [B, N, N] ancestor-or-self */
+  float sm_scale;
+  int32_t max_kv_len;
+  void* o; int64_t o_sb, o_sn, o_sh;            /* [B, N, Hq, D] bf16      */
+} dft_tree_attn_args;
+DFT_API int64_t dft_tree_attn_workspace_bytes(const dft_tree_attn_args* a);
+DFT_API int dft_tree_attn(const dft_tree_attn_args* a, void* workspace, int32_t* dev_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

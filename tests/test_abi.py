@@ -55,6 +55,8 @@ def test_invalid_arguments_are_rejected_on_the_host(lib):
     assert lib.dft_gdn_commit(None, None, None) == 1
     assert lib.dft_tree_conv(None, None, None) == 1
     assert lib.dft_conv_commit(None, None, None) == 1
+    assert lib.dft_tree_attn(None, None, None, None) == 1
+    assert lib.dft_tree_attn_workspace_bytes(None) == -1
     assert lib.dft_table_save(None, b"x", None) == 1
     assert lib.dft_table_load(None, None, None) == 1
     assert lib.dft_table_set_params(None, 20.0, 60.0, 20.0, 10.0) == 1
@@ -76,6 +78,9 @@ int main(void) {
   printf("dft_commit_args SIZE %zu\n", sizeof(dft_commit_args));
   printf("dft_conv_commit_args SIZE %zu\n", sizeof(dft_conv_commit_args));
   F(dft_conv_commit_args, cs_st) F(dft_conv_commit_args, last) F(dft_conv_commit_args, x_sn)
+  printf("dft_tree_attn_args SIZE %zu\n", sizeof(dft_tree_attn_args));
+  F(dft_tree_attn_args, q) F(dft_tree_attn_args, n_slots) F(dft_tree_attn_args, sm_scale)
+  F(dft_tree_attn_args, max_kv_len) F(dft_tree_attn_args, o) F(dft_tree_attn_args, o_sh)
   F(dft_table_desc, max_load) F(dft_table_desc, n4c) F(dft_build_params, lam_p)
   F(dft_conv_args, iw_slots) F(dft_conv_args, y_dtype) F(dft_gdn_args, ag_sh) F(dft_gdn_args, pool)
   F(dft_gdn_args, aux_k_per_v) F(dft_commit_args, ends) F(dft_commit_args, aux_k_per_v) F(dft_commit_args, so_sk)
@@ -95,7 +100,7 @@ def test_ctypes_layout_matches_header(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
     structs = {"dft_table_desc": L.TableDesc, "dft_build_params": L.BuildParams, "dft_tree_out": L.TreeOut,
                "dft_conv_args": L.ConvArgs, "dft_gdn_args": L.GdnArgs, "dft_commit_args": L.CommitArgs,
-               "dft_conv_commit_args": L.ConvCommitArgs}
+               "dft_conv_commit_args": L.ConvCommitArgs, "dft_tree_attn_args": L.TreeAttnArgs}
     for line in out:
         if not line:
             continue
