@@ -41,6 +41,12 @@ VERIFY_AUX_BYTES = 8192 * 3 * 2 + 262144 + 524288 + 4096               # conv st
 COMMIT_BYTES_FIXED = 4 * 1024 * 1024                                   # read S0 + write S
 COMMIT_BYTES_PER_NODE = 32 * 1024                                      # k, vn rows of 32 heads
 SCORE_BYTES = S * V * 4 + 105984 * 12 + 2944                           # logits + table probes + prev/pn
+# gated full-attention layers (config 3): 16 q-heads / 4 kv-heads at dim 256, 4K-token prefix + the tree
+ATTN_HQ, ATTN_HKV, ATTN_D, ATTN_PREFIX = 16, 4, 256, 4096
+ATTN_KEYS = ATTN_PREFIX + N
+# per layer-request: K and V of every key (bf16), q and o (bf16), the key slot indices (int32)
+ATTN_BYTES = ATTN_KEYS * ATTN_HKV * ATTN_D * 2 * 2 + 2 * N * ATTN_HQ * ATTN_D * 2 + ATTN_KEYS * 4
+ATTN_FLOPS = 4 * N * ATTN_HQ * ATTN_KEYS * ATTN_D
 
 
 def _peaks():
@@ -385,6 +391,8 @@ def run_ours(args, rank, world, local_rank):
             ems = float(tt)
         e2e = {"value": world * ke / (ems / 1e3), "unit": "cycles/s", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h), "steps": ke}
+    # ---- tree-masked attention verify of one gated full-attention layer (outside the cycle)
+    attn = _bench_attention(args, dev, cyc, g, stream) if args.attn else None
     status = int(cyc.status.item())
 
     if rank != 0:
@@ -416,6 +424,11 @@ def run_ours(args, rank, world, local_rank):
         "gdn_commit_GBps": commit_bytes / (commit_launch_ms / 1e3) / 1e9,
         "mean_accept_len": mean_acc,
     }
+    if attn is not None:
+        per_kernel["tree_attn_ms_per_layer"] = attn
+        per_kernel["tree_attn_GBps"] = Bt * ATTN_BYTES / (attn / 1e3) / 1e9
+        per_kernel["tree_attn_hbm_frac"] = per_kernel["tree_attn_GBps"] / hbm
+        per_kernel["tree_attn_TFLOPs"] = Bt * ATTN_FLOPS / (attn / 1e3) / 1e12
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "cycles/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
@@ -430,6 +443,38 @@ def run_ours(args, rank, world, local_rank):
         line["e2e"] = e2e
     line["clocks"] = clk.summary()
     return line
+
+
+def _bench_attention(args, dev, cyc, g, stream):
+    """Mean CUDA-event time of one tree-masked attention layer (attention +
+    split merge) over the batch: 4K-token prefixes in a paged KV cache with
+    shuffled slots (1.1 GB, larger than L2), the cycle's own trees as masks."""
+    import torch
+    from dforktree_b200.tree_attn import TreeAttentionWrapper
+    Bt = cyc.cfg.B
+    slots = Bt * ATTN_KEYS
+    perm = torch.randperm(slots, device=dev, generator=g).to(torch.int32)
+    kc = torch.randn(slots, ATTN_HKV, ATTN_D, device=dev, generator=g).to(torch.bfloat16)
+    vc = torch.randn(slots, ATTN_HKV, ATTN_D, device=dev, generator=g).to(torch.bfloat16)
+    q = torch.randn(Bt, N, ATTN_HQ, ATTN_D, device=dev, generator=g).to(torch.bfloat16)
+    indptr = (torch.arange(Bt + 1, device=dev) * ATTN_KEYS).to(torch.int32)
+    w = TreeAttentionWrapper(dev).plan(indptr, perm, ATTN_HQ, ATTN_HKV, ATTN_D, n=N, anc=cyc.tree["anc"],
+                                       kv_lens_host=[ATTN_KEYS] * Bt)
+    o = torch.empty_like(q)
+    for _ in range(max(args.warmup, 3)):
+        w.run(q, (kc, vc), out=o)
+    mk = lambda: torch.cuda.Event(enable_timing=True)
+    pairs = []
+    for _ in range(max(args.steps, 5)):
+        e1, e2 = mk(), mk()
+        e1.record(stream)
+        w.run(q, (kc, vc), out=o)
+        e2.record(stream)
+        pairs.append((e1, e2))
+    torch.cuda.synchronize()
+    if w.device_status():
+        raise RuntimeError(f"tree attention raised device status {w.device_status()}")
+    return sum(e1.elapsed_time(e2) for e1, e2 in pairs) / len(pairs)
 
 
 def _traffic():
@@ -472,6 +517,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-attn", dest="attn", action="store_false",
+                    help="skip the tree-masked attention stage (reported under stages, outside the cycle)")
     ap.add_argument("--profile", action="store_true", help="only W + K plain cycles (for ncu); prints nothing")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
