@@ -10,28 +10,29 @@
 // Here: one CTA per work unit (request b, kv-head h, key split s).  The G
 // q-heads of kv-head h and the N tree nodes form one 128-row query tile
 // (row = node * G + head), so one tcgen05 MMA of M = 128 serves the whole
-// group:
-//   Q   TMA (4-D tensor map, 128-byte swizzle) -> shared, once per unit
+// group.  Both A operands live in tensor memory, so shared memory holds only
+// the K / V stream:
+//   Q   loaded once per unit by the softmax threads (one row each) and stored
+//       to TMEM as packed bf16
 //   K,V 64-key tiles gathered through the page table (page size 1) with
-//       16-byte cp.async into the 128B-swizzled layout, two stages, four
-//       producer warps (the paged rows rule out tiled TMA)
-//   S   = Q K^T    tcgen05 kind::f16 (bf16 in, fp32 out), M=128 N=64 K=256, TMEM
+//       16-byte cp.async into the 128B-swizzled layout: three stages, four
+//       producer warps, the next tile's slot indices fetched a tile ahead
+//       (paged rows rule out tiled TMA)
+//   S   = Q K^T    tcgen05 kind::f16, A from TMEM, M=128 N=64 K=256, fp32 in TMEM
 //   P   = exp2(S * scale*log2e - m) with the tree mask, one thread per row
-//       (TMEM lane); running max rescales O in TMEM only when it grows by
-//       more than 2^8, P to shared as bf16 (K-major, swizzled)
-//   O  += P V      tcgen05 kind::f16, V as an MN-major operand, M=128 N=256 K=64
-// S is double-buffered in TMEM (O 256 columns + 2 x 64), so the S MMA of
-// tile t+1 runs while the softmax of tile t does.  Splits write (O, m, l)
-// partials that a second kernel merges; a single split writes o directly.
-// Every wait is bounded (~1 s); on timeout the CTA raises DFT_DEV_TIMEOUT,
-// drains its copies and MMAs (bounded), frees TMEM and exits.
+//       (TMEM lane); the running max moves (and O is rescaled in TMEM) only
+//       when it grows by more than 8; P written back as bf16 over its own S
+//   O  += P V      tcgen05 kind::f16, A = P from TMEM, V as an MN-major smem
+//       operand, M=128 N=256 K=64
+// S / P are double-buffered in TMEM (O 256 columns, Q 128, S/P 2 x 64), so
+// the S MMA of tile t+1 runs while the softmax of tile t does.  Splits write
+// (O, m, l) partials that a second kernel merges; a single split writes o
+// directly.  Every wait is bounded (~1 s); on timeout the CTA raises
+// DFT_DEV_TIMEOUT, drains its copies and MMAs (bounded), frees TMEM and exits.
 #include "dft_common.cuh"
 #include "dft_tc.cuh"
 
-#include <cuda.h>
-
 #include <cstring>
-#include <mutex>
 
 using namespace dft;
 using namespace dft::tc;
@@ -41,26 +42,23 @@ namespace {
 constexpr int kD = 256;        // head dim (tensor-core path)
 constexpr int kRows = 128;     // query rows per unit (nodes x group)
 constexpr int kKeys = 64;      // keys per tile
+constexpr int kStages = 3;     // K/V tiles in shared memory
 constexpr int kThreads = 288;  // warps 0-3 softmax / epilogue, 4 control + MMA, 5-8 KV producers
 constexpr int kProducers = 128;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t COL_O = 0, COL_S = 256;  // S buffer b at COL_S + 64 b
+constexpr uint32_t COL_O = 0, COL_Q = 256, COL_S = 384;  // S/P buffer b at COL_S + 64 b
 
-constexpr uint32_t kQChunk = kRows * 128;   // 16 KB: 128 rows x 64 dims
 constexpr uint32_t kKVChunk = kKeys * 128;  // 8 KB: 64 keys x 64 dims
 constexpr uint32_t kKVTile = 4 * kKVChunk;  // 32 KB
-constexpr uint32_t OFF_Q = 0;
-constexpr uint32_t OFF_KV = 64 * 1024;      // stage s: K at + 64 KB s, V at + 64 KB s + 32 KB
-constexpr uint32_t OFF_P = 192 * 1024;      // P buffer b at + 16 KB b
-constexpr uint32_t OFF_SMALL = 224 * 1024;
+constexpr uint32_t kStageBytes = 2 * kKVTile;  // K then V
+constexpr uint32_t OFF_SMALL = kStages * kStageBytes;
 constexpr uint32_t kSmallBytes = 512;
 constexpr uint32_t kSmem = OFF_SMALL + kSmallBytes + 1024;  // + alignment slack
 
 struct Small {
-  uint64_t q_full;
-  uint64_t kv_full[2], kv_empty[2];
-  uint64_t s_full[2], s_free[2];
-  uint64_t p_full[2], p_free[2];
+  uint64_t q_ready;
+  uint64_t kv_full[kStages], kv_empty[kStages];
+  uint64_t s_full[2], p_full[2];
   uint64_t o_done, mma_done;
   uint32_t tmem_base;
   int abort;
@@ -95,7 +93,7 @@ __device__ __forceinline__ void set_abort(Small& sm, int32_t* status) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    tree_attn_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ AttnParams P, int32_t* status) {
+    tree_attn_kernel(const __grid_constant__ AttnParams P, int32_t* status) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Small& sm = *reinterpret_cast<Small*>(smem + OFF_SMALL);
@@ -123,14 +121,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 4) {
     if (lane == 0) {
-      mbar_init(smem_u32(&sm.q_full), 1);
-      for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&sm.q_ready), kRows);
+      for (int i = 0; i < kStages; ++i) {
         mbar_init(smem_u32(&sm.kv_full[i]), kProducers);
         mbar_init(smem_u32(&sm.kv_empty[i]), 1);
+      }
+      for (int i = 0; i < 2; ++i) {
         mbar_init(smem_u32(&sm.s_full[i]), 1);
-        mbar_init(smem_u32(&sm.s_free[i]), kRows);
         mbar_init(smem_u32(&sm.p_full[i]), kRows);
-        mbar_init(smem_u32(&sm.p_free[i]), 1);
       }
       mbar_init(smem_u32(&sm.o_done), 1);
       mbar_init(smem_u32(&sm.mma_done), 1);
@@ -146,46 +144,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 4) {
-    // ------------------------------------------------ control: Q load + MMAs
+    // ------------------------------------------------------ control: MMAs
     if (lane == 0 && T > 0) {
-      const uint64_t pol = l2_evict_first();
-      const uint32_t qf = smem_u32(&sm.q_full);
-      mbar_expect_tx(qf, 4 * kQChunk);
-      for (int c = 0; c < 4; ++c) tma_load_4d(sbase + OFF_Q + c * kQChunk, &q_map, 64 * c, h * P.G, 0, b, qf, pol);
-      bool ok = mbar_wait_or_abort(qf, 0, abort_flag);
+      bool ok = mbar_wait_or_abort(smem_u32(&sm.q_ready), 0, abort_flag);
       const uint32_t id_s = idesc_bf16(128, kKeys, false), id_o = idesc_bf16(128, kD, true);
       for (int t = 0; ok && t <= T; ++t) {
         if (t < T) {
-          const int st = t & 1;
-          ok = mbar_wait_or_abort(smem_u32(&sm.kv_full[st]), (t >> 1) & 1, abort_flag);
-          if (ok && t >= 2) ok = mbar_wait_or_abort(smem_u32(&sm.s_free[st]), ((t >> 1) - 1) & 1, abort_flag);
+          const int st = t % kStages, sb = t & 1;
+          ok = mbar_wait_or_abort(smem_u32(&sm.kv_full[st]), (t / kStages) & 1, abort_flag);
+          // S/P buffer sb is free once P V of tile t-2 has retired
+          if (ok && t >= 2) ok = mbar_wait_or_abort(smem_u32(&sm.o_done), (t - 2) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
           fence_async_smem();  // cp.async (generic proxy) writes -> tensor-core reads
-          const uint32_t kb = sbase + OFF_KV + st * 2 * kKVTile;
+          const uint32_t kb = sbase + st * kStageBytes;
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
-            const uint64_t ad = sw128_desc(sbase + OFF_Q + (k >> 2) * kQChunk + (k & 3) * 32);
             const uint64_t bd = sw128_desc(kb + (k >> 2) * kKVChunk + (k & 3) * 32);
-            mma_bf16(tmem + COL_S + 64 * st, ad, bd, id_s, k > 0);
+            mma_bf16_ts(tmem + COL_S + 64 * sb, tmem + COL_Q + 8 * k, bd, id_s, k > 0);
           }
-          mma_commit(smem_u32(&sm.s_full[st]));
+          mma_commit(smem_u32(&sm.s_full[sb]));
         }
         if (t >= 1) {
           const int u = t - 1, pb = u & 1;
           ok = mbar_wait_or_abort(smem_u32(&sm.p_full[pb]), (u >> 1) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t vb = sbase + OFF_KV + (u & 1) * 2 * kKVTile + kKVTile;
+          const uint32_t vb = sbase + (u % kStages) * kStageBytes + kKVTile;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = sw128_desc(sbase + OFF_P + pb * kQChunk + k * 32);
             // V [keys x dims] is MN-major: 64-dim chunks 8 KB apart, 8-key groups 1 KB apart
             const uint64_t bd = sw128_desc(vb + k * 16 * 128, kKVChunk, 1024);
-            mma_bf16(tmem + COL_O, ad, bd, id_o, (u > 0 || k > 0) ? 1u : 0u);
+            mma_bf16_ts(tmem + COL_O, tmem + COL_S + 64 * pb + 8 * k, bd, id_o, (u > 0 || k > 0) ? 1u : 0u);
           }
-          mma_commit(smem_u32(&sm.kv_empty[u & 1]));
-          mma_commit(smem_u32(&sm.p_free[pb]));
+          mma_commit(smem_u32(&sm.kv_empty[u % kStages]));
           mma_commit(smem_u32(&sm.o_done));
         }
       }
@@ -203,32 +195,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     const unsigned char* vc = static_cast<const unsigned char*>(a.v_cache);
     const int64_t head_off = (int64_t)h * a.kv_sh * 2 + (int64_t)lane * 16;
     const uint32_t dst_lane = (uint32_t)(lane >> 3) * kKVChunk;
+    // lane i < 16 holds the slot of key 4 i + pw of a tile (-1 past the end)
+    auto fetch_slots = [&](int tile) -> int {
+      const int j = tile * kKeys + 4 * lane + pw;
+      return (lane < kKeys / 4 && j < len) ? a.kv_indices[kv_start + j] : -1;
+    };
+    int cur = T > 0 ? fetch_slots(t0) : -1;
     bool ok = true;
     for (int t = 0; t < T; ++t) {
-      const int st = t & 1;
-      if (t >= 2) {
-        ok = mbar_wait_or_abort(smem_u32(&sm.kv_empty[st]), ((t >> 1) - 1) & 1, abort_flag);
+      const int st = t % kStages;
+      const int nxt = t + 1 < T ? fetch_slots(t0 + t + 1) : -1;  // in flight during this tile
+      if (t >= kStages) {
+        ok = mbar_wait_or_abort(smem_u32(&sm.kv_empty[st]), (t / kStages - 1) & 1, abort_flag);
         if (!ok) break;
       }
-      const uint32_t kb = sbase + OFF_KV + st * 2 * kKVTile, vb = kb + kKVTile;
       const int j0 = (t0 + t) * kKeys;
-#pragma unroll 4
+      if (lane < kKeys / 4 && j0 + 4 * lane + pw < len && (cur < 0 || (int64_t)cur >= a.n_slots))
+        raise_status(status, DFT_DEV_BAD_INDEX);
+      const uint32_t kb = sbase + st * kStageBytes, vb = kb + kKVTile;
+#pragma unroll
       for (int kk = 0; kk < kKeys / 4; ++kk) {
         const int r = kk * 4 + pw;
-        const int j = j0 + r;
-        bool valid = j < len;
-        int64_t slot = valid ? (int64_t)a.kv_indices[kv_start + j] : 0;
-        if (valid && (slot < 0 || slot >= a.n_slots)) {
-          if (lane == 0) raise_status(status, DFT_DEV_BAD_INDEX);
-          valid = false;
-          slot = 0;
-        }
-        const int64_t off = slot * a.kv_st * 2 + head_off;
+        const int slot = __shfl_sync(0xffffffffu, cur, kk);
+        const bool valid = j0 + r < len && slot >= 0 && (int64_t)slot < a.n_slots;
+        const int64_t off = (int64_t)(valid ? slot : 0) * a.kv_st * 2 + head_off;
         const uint32_t dst = dst_lane + (uint32_t)r * 128 + ((((uint32_t)lane & 7) ^ ((uint32_t)r & 7)) << 4);
         cp_async16(kb + dst, valid ? kc + off : kc, valid ? 16u : 0u, pol);
         cp_async16(vb + dst, valid ? vc + off : vc, valid ? 16u : 0u, pol);
       }
       cp_async_arrive_noinc(smem_u32(&sm.kv_full[st]));
+      cur = nxt;
     }
     cp_async_wait_all();
     if (!ok && !*abort_flag) set_abort(sm, status);
@@ -237,6 +233,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = tid;  // TMEM lane r
     const int n = r / P.G, g = r % P.G;
     const bool row_ok = n < a.N;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // Q row -> TMEM (packed bf16, 128 columns); rows past the tree are zero
+    {
+      const uint4* qrow = reinterpret_cast<const uint4*>(
+          static_cast<const unsigned char*>(a.q) +
+          ((int64_t)b * a.q_sb + (int64_t)(row_ok ? n : 0) * a.q_sn + (int64_t)(h * P.G + g) * a.q_sh) * 2);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 u = row_ok ? __ldg(qrow + 8 * c + q) : make_uint4(0u, 0u, 0u, 0u);
+          v[4 * q] = __uint_as_float(u.x);
+          v[4 * q + 1] = __uint_as_float(u.y);
+          v[4 * q + 2] = __uint_as_float(u.z);
+          v[4 * q + 3] = __uint_as_float(u.w);
+        }
+        tmem_st32(tmem + lane_base + COL_Q + 32 * c, v);
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&sm.q_ready));
+    }
     uint64_t mask = 0;  // bit m: tree node m is n or an ancestor of n
     if (row_ok) {
       const float* arow = a.anc + (int64_t)b * a.anc_sb + (int64_t)n * a.N;
@@ -244,7 +262,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (__ldg(arow + m) > 0.5f) mask |= 1ull << m;
     }
     const float sc = a.sm_scale * 1.4426950408889634f;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     // tcgen05.ld / st are warp-collective: every branch around them is
     // warp-uniform (waits are reduced over the warp, the rescale decision too)
     float m_used = -INFINITY, l = 0.f;
@@ -264,8 +281,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[32 + i] = v[i];
       }
-      tc_fence_before();
-      mbar_arrive(smem_u32(&sm.s_free[sb]));
       const int j0 = (t0 + t) * kKeys;
       float tmax = -INFINITY;
 #pragma unroll
@@ -300,30 +315,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         m_used = m_new;
       }
-      uint32_t pk[32];
+      float pk[32];
       float sum = 0.f;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float p0 = x[2 * i] == -INFINITY ? 0.f : ex2(x[2 * i] - m_used);
         const float p1 = x[2 * i + 1] == -INFINITY ? 0.f : ex2(x[2 * i + 1] - m_used);
-        pk[i] = pack_bf16(p0, p1);
-        sum += bf16_lo(pk[i]) + bf16_hi(pk[i]);
+        const uint32_t w = pack_bf16(p0, p1);
+        sum += bf16_lo(w) + bf16_hi(w);
+        pk[i] = __uint_as_float(w);
       }
       l += sum;
-      const int pb = t & 1;
-      if (t >= 2) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait_or_abort(smem_u32(&sm.p_free[pb]), ((t >> 1) - 1) & 1, abort_flag));
-        if (!ok) break;
-      }
-      unsigned char* prow = smem + OFF_P + pb * kQChunk + r * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_async_smem();  // generic stores -> tensor-core reads
+      // P (bf16 pairs) over the first 32 columns of its own S buffer
+      tmem_st32(tmem + lane_base + COL_S + 64 * sb, pk);
       tc_fence_before();
-      mbar_arrive(smem_u32(&sm.p_full[pb]));
+      mbar_arrive(smem_u32(&sm.p_full[sb]));
     }
     // the last P V has retired once every MMA has (o_done's parity cannot tell
     // its final phase from the one before: the last S MMA precedes two P V)
@@ -408,22 +414,6 @@ __global__ void __launch_bounds__(64) tree_attn_combine(const __grid_constant__ 
 }
 
 // ------------------------------------------------------------------ host --
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
 int sm_count() {
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
@@ -486,7 +476,6 @@ extern "C" int64_t dft_tree_attn_workspace_bytes(const dft_tree_attn_args* a) {
 extern "C" int dft_tree_attn(const dft_tree_attn_args* a, void* workspace, int32_t* dev_status, void* stream) {
   const int rc = check_args(a);
   if (rc) return rc;
-  if (!encode_fn()) return DFT_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   AttnParams P;
   memset(&P, 0, sizeof(P));
@@ -500,21 +489,9 @@ extern "C" int dft_tree_attn(const dft_tree_attn_args* a, void* workspace, int32
     P.ws_ml = P.ws_o + units * kRows * kD;
   }
   if (units > 0x7FFFFFFF) return DFT_ERR_UNSUPPORTED;
-  CUtensorMap q_map;
-  {
-    // q as [B][N][Hq][D]: box = 64 dims x G heads x (128 / G) nodes; nodes >= N read as zeros
-    const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)a->Hq, (cuuint64_t)a->N, (cuuint64_t)a->B};
-    const cuuint64_t strides[3] = {(cuuint64_t)(a->q_sh * 2), (cuuint64_t)(a->q_sn * 2), (cuuint64_t)(a->q_sb * 2)};
-    const cuuint32_t box[4] = {64, (cuuint32_t)P.G, (cuuint32_t)(kRows / P.G), 1};
-    const cuuint32_t estr[4] = {1, 1, 1, 1};
-    if (encode_fn()(&q_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a->q), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return DFT_ERR_UNSUPPORTED;
-  }
   if (cudaFuncSetAttribute(tree_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) != cudaSuccess)
     return DFT_ERR_CUDA;
-  tree_attn_kernel<<<(unsigned)units, kThreads, kSmem, st>>>(q_map, P, dev_status);
+  tree_attn_kernel<<<(unsigned)units, kThreads, kSmem, st>>>(P, dev_status);
   DFT_LAUNCH_CHECK();
   if (P.splits > 1) {
     dim3 grid((unsigned)(a->N * a->Hq), (unsigned)a->B);
