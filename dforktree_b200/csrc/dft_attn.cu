@@ -43,7 +43,9 @@ constexpr int kD = 256;        // head dim (tensor-core path)
 constexpr int kRows = 128;     // query rows per unit (nodes x group)
 constexpr int kKeys = 64;      // keys per tile
 constexpr int kStages = 3;     // K/V tiles in shared memory
-constexpr int kThreads = 288;  // warps 0-3 softmax / epilogue, 4 control + MMA, 5-8 KV producers
+constexpr int kThreads = 416;  // warps 0-7 softmax / epilogue, 8 control + MMA, 9-12 KV producers
+constexpr int kSoftmax = 256;  // two threads per query row (columns split in halves)
+constexpr int kCtlWarp = 8, kProdWarp0 = 9;
 constexpr int kProducers = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t COL_O = 0, COL_Q = 256, COL_S = 384;  // S/P buffer b at COL_S + 64 b
@@ -52,7 +54,7 @@ constexpr uint32_t kKVChunk = kKeys * 128;  // 8 KB: 64 keys x 64 dims
 constexpr uint32_t kKVTile = 4 * kKVChunk;  // 32 KB
 constexpr uint32_t kStageBytes = 2 * kKVTile;  // K then V
 constexpr uint32_t OFF_SMALL = kStages * kStageBytes;
-constexpr uint32_t kSmallBytes = 512;
+constexpr uint32_t kSmallBytes = 4096;
 constexpr uint32_t kSmem = OFF_SMALL + kSmallBytes + 1024;  // + alignment slack
 
 struct Small {
@@ -62,6 +64,10 @@ struct Small {
   uint64_t o_done, mma_done;
   uint32_t tmem_base;
   int abort;
+  float xmax[2][2][kRows];  // [tile parity][half][row] tile max exchange between a row's two threads
+  float lsum[2][kRows];     // [half][row] final row sums
+  int okx[2][2][4];         // [tile parity][half][row warp] wait outcomes, shared by a row's two warps
+  int okr[2][2][4];         // the same for the rescale's wait
 };
 static_assert(sizeof(Small) <= kSmallBytes, "small region");
 
@@ -84,8 +90,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
-__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
-__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
 __device__ __forceinline__ void set_abort(Small& sm, int32_t* status) {
   *reinterpret_cast<volatile int*>(&sm.abort) = 1;
@@ -119,16 +123,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t1 = min(t0 + P.tps, n_tiles);
   const int T = t1 > t0 ? t1 - t0 : 0;
 
-  if (warp == 4) {
+  if (warp == kCtlWarp) {
     if (lane == 0) {
-      mbar_init(smem_u32(&sm.q_ready), kRows);
+      mbar_init(smem_u32(&sm.q_ready), kSoftmax);
       for (int i = 0; i < kStages; ++i) {
         mbar_init(smem_u32(&sm.kv_full[i]), kProducers);
         mbar_init(smem_u32(&sm.kv_empty[i]), 1);
       }
       for (int i = 0; i < 2; ++i) {
         mbar_init(smem_u32(&sm.s_full[i]), 1);
-        mbar_init(smem_u32(&sm.p_full[i]), kRows);
+        mbar_init(smem_u32(&sm.p_full[i]), kSoftmax);
       }
       mbar_init(smem_u32(&sm.o_done), 1);
       mbar_init(smem_u32(&sm.mma_done), 1);
@@ -143,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp == 4) {
+  if (warp == kCtlWarp) {
     // ------------------------------------------------------ control: MMAs
     if (lane == 0 && T > 0) {
       bool ok = mbar_wait_or_abort(smem_u32(&sm.q_ready), 0, abort_flag);
@@ -187,9 +191,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(smem_u32(&sm.mma_done), 0)) raise_status(status, DFT_DEV_TIMEOUT);
     }
     __syncwarp();
-  } else if (warp >= 5) {
+  } else if (warp >= kProdWarp0) {
     // ------------------------------------------- producers: paged K/V gather
-    const int p = tid - 160, pw = p >> 5;
+    const int pw = warp - kProdWarp0;
     const uint64_t pol = l2_evict_first();
     const unsigned char* kc = static_cast<const unsigned char*>(a.k_cache);
     const unsigned char* vc = static_cast<const unsigned char*>(a.v_cache);
@@ -229,18 +233,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     cp_async_wait_all();
     if (!ok && !*abort_flag) set_abort(sm, status);
   } else {
-    // ------------------------------------- softmax / epilogue: one row each
-    const int r = tid;  // TMEM lane r
+    // ---------------------- softmax / epilogue: two threads per row, one half each
+    const int r = (warp & 3) * 32 + lane;  // TMEM lane (query row)
+    const int hf = warp >> 2;              // S columns [32 hf, 32 hf + 32), O / Q columns by halves
+    const int pair_bar = 1 + (warp & 3);   // named barrier of warps w and w + 4 (same rows)
     const int n = r / P.G, g = r % P.G;
     const bool row_ok = n < a.N;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    // Q row -> TMEM (packed bf16, 128 columns); rows past the tree are zero
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    // Q row half -> TMEM (packed bf16, 64 columns); rows past the tree are zero
     {
       const uint4* qrow = reinterpret_cast<const uint4*>(
           static_cast<const unsigned char*>(a.q) +
-          ((int64_t)b * a.q_sb + (int64_t)(row_ok ? n : 0) * a.q_sn + (int64_t)(h * P.G + g) * a.q_sh) * 2);
+          ((int64_t)b * a.q_sb + (int64_t)(row_ok ? n : 0) * a.q_sn + (int64_t)(h * P.G + g) * a.q_sh) * 2 +
+          hf * 256);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float v[32];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -250,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           v[4 * q + 2] = __uint_as_float(u.z);
           v[4 * q + 3] = __uint_as_float(u.w);
         }
-        tmem_st32(tmem + lane_base + COL_Q + 32 * c, v);
+        tmem_st32(tmem + lane_base + COL_Q + 64 * hf + 32 * c, v);
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&sm.q_ready));
@@ -263,71 +270,107 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const float sc = a.sm_scale * 1.4426950408889634f;
     // tcgen05.ld / st are warp-collective: every branch around them is
-    // warp-uniform (waits are reduced over the warp, the rescale decision too)
+    // warp-uniform (waits are reduced over the warp, the rescale decision
+    // too); a row's two threads see the same tile max and so decide alike
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
+    // A row's two warps meet at the same named barriers in the same order;
+    // every early exit is decided from outcomes both have exchanged there.
+    const int wq = warp & 3;
     for (int t = 0; t < T; ++t) {
       const int sb = t & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(smem_u32(&sm.s_full[sb]), (t >> 1) & 1, abort_flag));
-      if (!ok) break;
-      tc_fence_after();
-      float x[64];
-      {
-        float v[32];
-        tmem_ld32(tmem + lane_base + COL_S + 64 * sb, v);
+      const bool got = __all_sync(0xffffffffu, mbar_wait_or_abort(smem_u32(&sm.s_full[sb]), (t >> 1) & 1, abort_flag));
+      float x[32];
+      if (got) {
+        tc_fence_after();
+        tmem_ld32(tmem + lane_base + COL_S + 64 * sb + 32 * hf, x);
+      } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[i] = v[i];
-        tmem_ld32(tmem + lane_base + COL_S + 64 * sb + 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) x[32 + i] = v[i];
+        for (int i = 0; i < 32; ++i) x[i] = 0.f;
       }
-      const int j0 = (t0 + t) * kKeys;
+      const int j0 = (t0 + t) * kKeys + 32 * hf;
+      // keys of a tile inside the prefix need no mask: x stays raw, P = 2^(x sc - m)
+      const bool plain = (t0 + t + 1) * kKeys <= plen;  // block-uniform
       float tmax = -INFINITY;
+      if (plain) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const int j = j0 + i;
-        float y = x[i] * sc;
-        if (j >= len) y = -INFINITY;
-        else if (j >= plen && !((mask >> (j - plen)) & 1ull)) y = -INFINITY;
-        x[i] = y;
-        tmax = fmaxf(tmax, y);
+        for (int i = 0; i < 32; ++i) tmax = fmaxf(tmax, x[i]);
+        tmax *= sc;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int j = j0 + i;
+          float y = x[i] * sc;
+          if (j >= len) y = -INFINITY;
+          else if (j >= plen && !((mask >> (j - plen)) & 1ull)) y = -INFINITY;
+          x[i] = y;
+          tmax = fmaxf(tmax, y);
+        }
       }
+      sm.xmax[sb][hf][r] = tmax;
+      if (lane == 0) sm.okx[sb][hf][wq] = got;
+      // the barrier also orders this half's S reads before the other half's P
+      // stores (half 1 writes P over S columns 16..31, which half 0 reads)
+      tc_fence_before();
+      named_bar(pair_bar, 64);
+      tc_fence_after();
+      tmax = fmaxf(tmax, sm.xmax[sb][hf ^ 1][r]);
+      ok = got && sm.okx[sb][hf ^ 1][wq];
+      if (!ok) break;
       // a row moves its reference max only when the tile max exceeds it by
       // more than 8 (P <= 2^8 otherwise); O then scales by 2^(old - new)
       const bool grow = tmax > m_used + 8.f;
       if (__any_sync(0xffffffffu, grow)) {
         const float m_new = grow ? tmax : m_used;
         if (t > 0) {
-          // O holds P V of tiles < t: wait for the last of them, then rescale
-          ok = __all_sync(0xffffffffu, mbar_wait_or_abort(smem_u32(&sm.o_done), (t - 1) & 1, abort_flag));
+          // O holds P V of tiles < t: wait for the last of them, then rescale this half row
+          const bool done = __all_sync(0xffffffffu,
+                                       mbar_wait_or_abort(smem_u32(&sm.o_done), (t - 1) & 1, abort_flag));
+          if (lane == 0) sm.okr[sb][hf][wq] = done;
+          named_bar(pair_bar, 64);
+          ok = done && sm.okr[sb][hf ^ 1][wq];
           if (!ok) break;
           tc_fence_after();
           const float alpha = grow ? ex2(m_used - m_new) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
+          for (int c = 0; c < 4; ++c) {
             float v[32];
-            tmem_ld32(tmem + lane_base + COL_O + 32 * c, v);
+            tmem_ld32(tmem + lane_base + COL_O + 128 * hf + 32 * c, v);
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= alpha;
-            tmem_st32(tmem + lane_base + COL_O + 32 * c, v);
+            tmem_st32(tmem + lane_base + COL_O + 128 * hf + 32 * c, v);
           }
           l *= alpha;
         }
         m_used = m_new;
       }
-      float pk[32];
-      float sum = 0.f;
+      uint32_t pk[16];
+      f32x2 sum2 = pk2(0.f, 0.f);
+      if (plain) {
+        const f32x2 sc2 = pk2(sc, sc), nm2 = pk2(-m_used, -m_used);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = x[2 * i] == -INFINITY ? 0.f : ex2(x[2 * i] - m_used);
-        const float p1 = x[2 * i + 1] == -INFINITY ? 0.f : ex2(x[2 * i + 1] - m_used);
-        const uint32_t w = pack_bf16(p0, p1);
-        sum += bf16_lo(w) + bf16_hi(w);
-        pk[i] = __uint_as_float(w);
+        for (int i = 0; i < 16; ++i) {
+          float e0, e1;
+          upk2(fma2(pk2(x[2 * i], x[2 * i + 1]), sc2, nm2), e0, e1);
+          const f32x2 p2 = pk2(ex2(e0), ex2(e1));
+          sum2 = add2(sum2, p2);
+          pk[i] = f32x2_to_bf16x2(p2);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = x[2 * i] == -INFINITY ? 0.f : ex2(x[2 * i] - m_used);
+          const float p1 = x[2 * i + 1] == -INFINITY ? 0.f : ex2(x[2 * i + 1] - m_used);
+          const f32x2 p2 = pk2(p0, p1);
+          sum2 = add2(sum2, p2);
+          pk[i] = f32x2_to_bf16x2(p2);
+        }
       }
-      l += sum;
-      // P (bf16 pairs) over the first 32 columns of its own S buffer
-      tmem_st32(tmem + lane_base + COL_S + 64 * sb, pk);
+      float s0, s1;
+      upk2(sum2, s0, s1);
+      l += s0 + s1;
+      // P (bf16 pairs) over columns [16 hf, 16 hf + 16) of its own S buffer
+      tmem_st16(tmem + lane_base + COL_S + 64 * sb + 16 * hf, pk);
       tc_fence_before();
       mbar_arrive(smem_u32(&sm.p_full[sb]));
     }
@@ -336,16 +379,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && T > 0) ok = __all_sync(0xffffffffu, mbar_wait_or_abort(smem_u32(&sm.mma_done), 0, abort_flag));
     if (!ok && !*abort_flag) set_abort(sm, status);
     tc_fence_after();
+    sm.lsum[hf][r] = l;
+    named_bar(pair_bar, 64);
+    l = sm.lsum[0][r] + sm.lsum[1][r];
     const bool have = ok && T > 0;  // warp-uniform
     if (P.splits == 1) {
       if (have) {
         const float inv = l > 0.f ? 1.f / l : 0.f;
         unsigned char* orow = static_cast<unsigned char*>(a.o) +
-                              ((int64_t)b * a.o_sb + (int64_t)n * a.o_sn + (int64_t)(h * P.G + g) * a.o_sh) * 2;
+                              ((int64_t)b * a.o_sb + (int64_t)n * a.o_sn + (int64_t)(h * P.G + g) * a.o_sh) * 2 +
+                              hf * 256;
 #pragma unroll 1
-        for (int c = 0; c < kD / 32; ++c) {
+        for (int c = 0; c < 4; ++c) {
           float v[32];
-          tmem_ld32(tmem + lane_base + COL_O + 32 * c, v);
+          tmem_ld32(tmem + lane_base + COL_O + 128 * hf + 32 * c, v);
           if (row_ok) {
             uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
 #pragma unroll
@@ -359,24 +406,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
       const int64_t prow = (int64_t)unit * kRows + r;
-      float4* dst = reinterpret_cast<float4*>(P.ws_o + prow * kD);
+      float4* dst = reinterpret_cast<float4*>(P.ws_o + prow * kD + 128 * hf);
       const bool mine = have && l > 0.f;
 #pragma unroll 1
-      for (int c = 0; c < kD / 32; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float v[32];
-        if (have) tmem_ld32(tmem + lane_base + COL_O + 32 * c, v);
+        if (have) tmem_ld32(tmem + lane_base + COL_O + 128 * hf + 32 * c, v);
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           dst[8 * c + q] = mine ? make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3])
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      P.ws_ml[2 * prow] = mine ? m_used : -INFINITY;
-      P.ws_ml[2 * prow + 1] = mine ? l : 0.f;
+      if (hf == 0) {
+        P.ws_ml[2 * prow] = mine ? m_used : -INFINITY;
+        P.ws_ml[2 * prow + 1] = mine ? l : 0.f;
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kCtlWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
