@@ -263,10 +263,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(smem_u32(&sm.q_ready));
     }
     uint64_t mask = 0;  // bit m: tree node m is n or an ancestor of n
-    if (row_ok) {
-      const float* arow = a.anc + (int64_t)b * a.anc_sb + (int64_t)n * a.N;
-      for (int m = 0; m < a.N; ++m)
-        if (__ldg(arow + m) > 0.5f) mask |= 1ull << m;
+    {
+      // all loads issued before the first use (one memory latency, not N)
+      const float* arow = a.anc + (int64_t)b * a.anc_sb + (int64_t)(row_ok ? n : 0) * a.N;
+      float av[64];
+#pragma unroll
+      for (int m = 0; m < 64; ++m) av[m] = (row_ok && m < a.N) ? __ldg(arow + m) : 0.f;
+#pragma unroll
+      for (int m = 0; m < 64; ++m) mask |= (uint64_t)(av[m] > 0.5f) << m;
     }
     const float sc = a.sm_scale * 1.4426950408889634f;
     // tcgen05.ld / st are warp-collective: every branch around them is
