@@ -65,24 +65,38 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args
     }
   }
   if (tid < 32) {
-    // path nodes that are ancestors-or-self of u, in path order (fc1_fused.py:30-35):
-    // lane t looks at path entries t and t + 32, a ballot compacts them in order
+    // path nodes that are ancestors-or-self of u, in path order (fc1_fused.py:30-35).
+    // The ancestor row of u, the gate row (two entries per lane, N <= 64) and the
+    // path entries (t and t + 32, P <= 64) are loaded at once; a path node's
+    // ancestor flag and gate come from the lane holding them (no dependent
+    // global loads); a ballot compacts the kept nodes in order.
     const float* anc_u = a.anc + ((int64_t)b * a.N + u) * a.N;
+    const float an0 = tid < a.N ? anc_u[tid] : 0.f, an1 = tid + 32 < a.N ? anc_u[tid + 32] : 0.f;
+    const float g0 = tid < a.N ? G[tid] : 0.f, g1 = tid + 32 < a.N ? G[tid + 32] : 0.f;
+    int64_t pid[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int t = 32 * j + tid;
+      pid[j] = t < a.P ? a.path[(int64_t)b * a.P + t] : -1;
+      if (pid[j] >= a.N) {
+        raise_status(st, DFT_DEV_BAD_INDEX);
+        pid[j] = -1;
+      }
+    }
     const int cap_n = a.P < a.N ? a.P : a.N;
     int base = 0;
-    for (int t0 = 0; t0 < a.P; t0 += 32) {
-      const int t = t0 + tid;
-      int64_t id = t < a.P ? a.path[(int64_t)b * a.P + t] : -1;
-      if (id >= a.N) {
-        raise_status(st, DFT_DEV_BAD_INDEX);
-        id = -1;
-      }
-      const bool keep = id >= 0 && anc_u[id] > 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int64_t id = pid[j];
+      const int src = (int)(id & 31);
+      const float alo = __shfl_sync(0xffffffffu, an0, src), ahi = __shfl_sync(0xffffffffu, an1, src);
+      const float glo = __shfl_sync(0xffffffffu, g0, src), ghi = __shfl_sync(0xffffffffu, g1, src);
+      const bool keep = id >= 0 && (id >= 32 ? ahi : alo) > 0.f;
       const uint32_t m = __ballot_sync(0xffffffffu, keep);
       const int pos = base + __popc(m & ((1u << tid) - 1u));
       if (keep && pos < cap_n) {
         s_ids[pos] = (int)id;
-        s_w[pos] = expf(gu - G[id]);
+        s_w[pos] = expf(gu - (id >= 32 ? ghi : glo));
       }
       base += __popc(m);
     }

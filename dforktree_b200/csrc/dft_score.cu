@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kThreads) score_kernel(const T* __restrict__ l
   // vector body: every loop bound is block-uniform (warp-synchronous inserts)
   const int stride = kThreads * 4;  // elements per block-wide vector sweep
   int64_t base = head;
+  bool first = true;
   for (; base + 4 * stride <= body_end; base += 4 * stride) {
     const int64_t e = base + (int64_t)tid * 4;
     float4 vs[4];
@@ -148,6 +149,22 @@ __global__ void __launch_bounds__(kThreads) score_kernel(const T* __restrict__ l
     for (int r = 0; r < 4; ++r) vs[r] = load4<T>(x, e + r * stride);
 #pragma unroll
     for (int r = 0; r < 4; ++r) online_add4(m, sum, vs[r]);
+    if (first) {
+      // Seed the pruning bound from the first sweep: if at least 16 lanes hold a
+      // value >= v, the row's 16th largest is >= v, so smaller values can never
+      // enter the top 16.  v = the largest lane maximum with that property.
+      first = false;
+      float lm = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) lm = fmaxf(lm, fmaxf(fmaxf(vs[r].x, vs[r].y), fmaxf(vs[r].z, vs[r].w)));
+      int ge = 0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ge += __shfl_sync(0xffffffffu, lm, j) >= lm;
+      float seed = ge >= kTopM ? lm : -INFINITY;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) seed = fmaxf(seed, __shfl_xor_sync(0xffffffffu, seed, o));
+      bound = fmaxf(bound, seed);
+    }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       float mx = fmaxf(fmaxf(vs[r].x, vs[r].y), fmaxf(vs[r].z, vs[r].w));
