@@ -445,36 +445,63 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
-def _bench_attention(args, dev, cyc, g, stream):
-    """Mean CUDA-event time of one tree-masked attention layer (attention +
-    split merge) over the batch: 4K-token prefixes in a paged KV cache with
-    shuffled slots (1.1 GB, larger than L2), the cycle's own trees as masks."""
+def _attention_inputs(dev, Bt, anc, g):
+    """The attention workload of one gated full-attention layer: 4K-token
+    prefixes + the tree in a paged KV cache with shuffled slots (1.1 GB at
+    batch 64, larger than L2), planned once."""
     import torch
     from dforktree_b200.tree_attn import TreeAttentionWrapper
-    Bt = cyc.cfg.B
     slots = Bt * ATTN_KEYS
     perm = torch.randperm(slots, device=dev, generator=g).to(torch.int32)
     kc = torch.randn(slots, ATTN_HKV, ATTN_D, device=dev, generator=g).to(torch.bfloat16)
     vc = torch.randn(slots, ATTN_HKV, ATTN_D, device=dev, generator=g).to(torch.bfloat16)
     q = torch.randn(Bt, N, ATTN_HQ, ATTN_D, device=dev, generator=g).to(torch.bfloat16)
     indptr = (torch.arange(Bt + 1, device=dev) * ATTN_KEYS).to(torch.int32)
-    w = TreeAttentionWrapper(dev).plan(indptr, perm, ATTN_HQ, ATTN_HKV, ATTN_D, n=N, anc=cyc.tree["anc"],
+    w = TreeAttentionWrapper(dev).plan(indptr, perm, ATTN_HQ, ATTN_HKV, ATTN_D, n=N, anc=anc,
                                        kv_lens_host=[ATTN_KEYS] * Bt)
-    o = torch.empty_like(q)
+    return w, q, (kc, vc), torch.empty_like(q)
+
+
+def _bench_attention(args, dev, cyc, g, stream):
+    """Mean CUDA-event time of one tree-masked attention layer (attention +
+    split merge) over the batch, the cycle's own trees as masks."""
+    import torch
+    w, q, kv, o = _attention_inputs(dev, cyc.cfg.B, cyc.tree["anc"], g)
     for _ in range(max(args.warmup, 3)):
-        w.run(q, (kc, vc), out=o)
+        w.run(q, kv, out=o)
     mk = lambda: torch.cuda.Event(enable_timing=True)
     pairs = []
     for _ in range(max(args.steps, 5)):
         e1, e2 = mk(), mk()
         e1.record(stream)
-        w.run(q, (kc, vc), out=o)
+        w.run(q, kv, out=o)
         e2.record(stream)
         pairs.append((e1, e2))
     torch.cuda.synchronize()
     if w.device_status():
         raise RuntimeError(f"tree attention raised device status {w.device_status()}")
     return sum(e1.elapsed_time(e2) for e1, e2 in pairs) / len(pairs)
+
+
+def run_profile_attention(args):
+    """--profile-attn: W + K attention layers alone at the bench's shape (for ncu); prints nothing."""
+    import torch
+    from dforktree_b200 import build as B
+    from dforktree_b200 import kernels as K
+    B.build()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    Bt = args.batch
+    par = torch.zeros(Bt, N, dtype=torch.int64, device=dev)
+    par[:, 1:] = torch.randint(0, 1 << 30, (Bt, N - 1), device=dev, generator=g) % torch.arange(1, N, device=dev)
+    anc = K.tree_struct(par)[0]
+    w, q, kv, o = _attention_inputs(dev, Bt, anc, g)
+    for _ in range(args.warmup + args.steps):
+        w.run(q, kv, out=o)
+    torch.cuda.synchronize()
+    if w.device_status():
+        raise RuntimeError(f"tree attention raised device status {w.device_status()}")
 
 
 def _traffic():
@@ -520,7 +547,12 @@ def main():
     ap.add_argument("--no-attn", dest="attn", action="store_false",
                     help="skip the tree-masked attention stage (reported under stages, outside the cycle)")
     ap.add_argument("--profile", action="store_true", help="only W + K plain cycles (for ncu); prints nothing")
+    ap.add_argument("--profile-attn", action="store_true",
+                    help="only W + K tree-attention layers at the bench shape (for ncu); prints nothing")
     args = ap.parse_args()
+    if args.profile_attn:
+        run_profile_attention(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -7,6 +7,8 @@
 // fastest so every load and store is coalesced.
 #include "dft_common.cuh"
 
+#include <cstring>
+
 using namespace dft;
 
 namespace {
@@ -91,14 +93,74 @@ __global__ void conv_commit_kernel(dft_conv_commit_args a, int32_t* st) {
   for (int j = 0; j < 3; ++j) store_any(a.conv_state, a.cs_dtype, sbase + j * a.cs_st, v[j]);
 }
 
+// Packed form for bf16 states in the [.., C, 3] layout and bf16 inputs: one
+// thread per 8 channels reads their 48-byte state block and the 16-byte input
+// rows its taps name, and writes the 48-byte block back (all accesses 16-byte).
+__global__ void conv_commit_packed_kernel(dft_conv_commit_args a, int32_t* st) {
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int b = blockIdx.y, l = blockIdx.z;
+  if (c0 >= a.C) return;
+  const int64_t u = a.last[b];
+  if (u < 0) return;
+  if (u >= a.N) {
+    if (c0 == 0) raise_status(st, DFT_DEV_BAD_INDEX);
+    return;
+  }
+  const int64_t slot = a.slots ? a.slots[b] : b;
+  uint4* sp = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.conv_state) + (int64_t)l * a.cs_sl + slot * a.cs_ss +
+                                       (int64_t)c0 * 3);
+  const uint4 o0 = sp[0], o1 = sp[1], o2 = sp[2];
+  uint16_t old[24], out[24];
+  memcpy(old, &o0, 16);
+  memcpy(old + 8, &o1, 16);
+  memcpy(old + 16, &o2, 16);
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int64_t col = a.cidx[((int64_t)b * a.N + u) * 4 + j + 1];
+    if (col < 0 || col >= 3 + a.N) {
+      raise_status(st, DFT_DEV_BAD_INDEX);
+      return;
+    }
+    if (col < 3) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)  // register selects, no indexing by a runtime column
+        out[3 * e + j] = col == 0 ? old[3 * e] : (col == 1 ? old[3 * e + 1] : old[3 * e + 2]);
+    } else {
+      const uint4 xv = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) + (int64_t)l * a.x_sl +
+                                                       (int64_t)b * a.x_sb + (col - 3) * a.x_sn + c0);
+      uint16_t xr[8];
+      memcpy(xr, &xv, 16);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) out[3 * e + j] = xr[e];
+    }
+  }
+  uint4 n0, n1, n2;
+  memcpy(&n0, out, 16);
+  memcpy(&n1, out + 8, 16);
+  memcpy(&n2, out + 16, 16);
+  sp[0] = n0;
+  sp[1] = n1;
+  sp[2] = n2;
+}
+
 }  // namespace
 
 extern "C" int dft_conv_commit(const dft_conv_commit_args* a, int32_t* dev_status, void* stream) {
   if (!a || !a->x || !a->conv_state || !a->cidx || !a->last) return DFT_ERR_INVALID;
   if (a->L <= 0 || a->B <= 0 || a->N <= 0 || a->C <= 0 || a->B > 65535 || a->L > 65535) return DFT_ERR_INVALID;
   if (!valid_dtype(a->x_dtype) || !valid_dtype(a->cs_dtype)) return DFT_ERR_INVALID;
-  dim3 grid((a->C + 255) / 256, a->B, a->L);
-  conv_commit_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*a, dev_status);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool packed = a->cs_dtype == DFT_BF16 && a->x_dtype == DFT_BF16 && a->cs_st == 1 && a->cs_sc == 3 &&
+                      a->C % 8 == 0 && ((uintptr_t)a->conv_state & 15) == 0 && ((uintptr_t)a->x & 15) == 0 &&
+                      a->cs_sl % 8 == 0 && a->cs_ss % 8 == 0 && a->x_sl % 8 == 0 && a->x_sb % 8 == 0 &&
+                      a->x_sn % 8 == 0;
+  if (packed) {
+    dim3 grid((a->C / 8 + 255) / 256, a->B, a->L);
+    conv_commit_packed_kernel<<<grid, 256, 0, st>>>(*a, dev_status);
+  } else {
+    dim3 grid((a->C + 255) / 256, a->B, a->L);
+    conv_commit_kernel<<<grid, 256, 0, st>>>(*a, dev_status);
+  }
   DFT_LAUNCH_CHECK();
   return DFT_OK;
 }

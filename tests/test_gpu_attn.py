@@ -156,3 +156,27 @@ def test_wrapper_plan_run_with_plugin_custom_mask():
     torch.cuda.synchronize()
     assert o.shape == (64, 16, 256) and w.device_status() == 0
     assert _rel(_np(o).reshape(2, 32, 16, 256), _ref(c)) < TOL
+
+
+@pytest.mark.skipif(__import__("os").environ.get("DFT_TEST_FLASHINFER") != "1",
+                    reason="opt-in (DFT_TEST_FLASHINFER=1): JIT-builds flashinfer's prefill kernel on the box")
+def test_tree_attention_matches_flashinfer_custom_mask():
+    """Pin against the library the reference plugin verifies through: flashinfer's
+    paged prefill (fa2, page size 1) planned as fc1_plan.py:16-33 plans it, with
+    the fc1_branch64.py:39 mask [ones(n, prefix) | anc], one request per plan."""
+    flashinfer = pytest.importorskip("flashinfer")
+    B, N, HQ, HKV, D = 2, 32, 16, 4, 256
+    c = _case(B, N, HQ, HKV, [700, 45], seed=31)
+    ours = _np(_run(c))
+    ws = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=DEV)
+    for b in range(B):
+        lo, hi = int(c["indptr"][b]), int(c["indptr"][b + 1])
+        Lb = hi - lo
+        mask = torch.cat((torch.ones(N, Lb - N, dtype=torch.bool, device=DEV), c["anc"][b].bool()), 1).flatten()
+        w = flashinfer.BatchPrefillWithPagedKVCacheWrapper(ws, "NHD", backend="fa2")
+        w.plan(torch.tensor([0, N], dtype=torch.int32, device=DEV), torch.tensor([0, Lb], dtype=torch.int32, device=DEV),
+               c["indices"][lo:hi].to(torch.int32), torch.ones(1, dtype=torch.int32, device=DEV), HQ, HKV, D, 1,
+               custom_mask=mask, q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16)
+        ref = w.run(c["q"][b], (c["k"].unsqueeze(1), c["v"].unsqueeze(1)))
+        torch.cuda.synchronize()
+        assert _rel(ours[b], _np(ref)) < TOL, (b, _rel(ours[b], _np(ref)))

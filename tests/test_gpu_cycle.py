@@ -185,14 +185,15 @@ def test_cycle_step_matches_oracle_chain():
             np.testing.assert_array_equal(_np(cyc.conv_state[l, r]), np.stack(src, 1))
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_conv_commit_slots_skips_and_bad_index(dtype):
+@pytest.mark.parametrize("dtype,C", [(torch.float32, 1000), (torch.bfloat16, 1000), (torch.bfloat16, 1024)])
+def test_conv_commit_slots_skips_and_bad_index(dtype, C):
     """Conv-window commit through the C ABI: per layer and request the state
     takes taps 1..3 of node last[b] (state columns or new inputs, by cidx);
-    last < 0 leaves it untouched; slots map requests to pool rows."""
+    last < 0 leaves it untouched; slots map requests to pool rows.  bf16 with
+    C % 8 == 0 runs the packed 16-byte kernel, the rest the general one."""
     from dforktree_b200 import kernels as K
     from dforktree_b200 import synth
-    Ls, B, N, C, slots_n = 3, 5, 32, 1000, 9
+    Ls, B, N, slots_n = 3, 5, 32, 9
     rng = np.random.default_rng(21)
     cidx = np.stack([OB.tree_struct(synth.random_tree_parents(N, rng), 4)[2] for _ in range(B)])
     g = torch.Generator(device=DEV)
