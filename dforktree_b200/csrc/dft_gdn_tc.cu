@@ -102,8 +102,8 @@ __device__ __forceinline__ float bits_f32(uint32_t v, int dtype) {
 __device__ __forceinline__ uint32_t anc_mask_warp(const float* anc, int b, int N, int lane) {
   uint32_t mine = 0;
   const float* base = anc + (int64_t)b * N * N;
-  // eight rows per step, two steps in flight
-#pragma unroll 2
+  // eight rows per step, all four steps in flight (one memory latency)
+#pragma unroll
   for (int n0 = 0; n0 < kNP; n0 += 8) {
     float v[8];
 #pragma unroll
