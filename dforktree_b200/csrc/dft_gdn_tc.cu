@@ -7,18 +7,22 @@
 // Here: one persistent CTA per SM loops over work units (request, k-head);
 // a unit covers the R <= 2 v-heads sharing that k-head, and both heads run
 // side by side on disjoint warps and buffers.  Per unit:
-//   F  the unit's bf16 activation tile (pre-conv x, or y) is already in
-//      shared memory (TMA, issued during the previous unit).  Tree conv in
+//   F  the unit's bf16 activation tile (pre-conv x, or y) is in shared memory
+//      and already converted: the first unit's arrives by TMA and is
+//      converted at the top of the loop; every later unit's is gathered by
+//      the conv threads (16-byte cp.async) and converted at the end of the
+//      previous unit, while warps 8+ run that unit's M2 and E2.  Tree conv in
 //      place, one thread per channel pair in packed fp32x2 arithmetic, nodes
 //      from last to first (a node's taps are its ancestors, lower indices);
 //      then one warp per node pair: L2 norms of q / k, the swizzled tf32
-//      operand [k; q] and the fp32 k_hat rows (stored to aux_k); gates and
-//      ancestor masks by three other warps
+//      operand [k; q] and the fp32 k_hat rows (stored to aux_k).  The next
+//      unit's gates and ancestor masks are computed by warps 0, 1, 4 during
+//      this unit's X / Z solves
 //   M0 tcgen05 MMA  D0 = [k; q] k^T          -> k.k^T and q.k^T  (TMEM)
 //   M1 tcgen05 MMA  D1_h = S0_h [k; q]^T     -> (k S0)^T, (q S0)^T per v-head;
-//      the heads' states share one 64 KB slot, streamed HBM -> shared by TMA
-//      (128B swizzle, no multicast): head 1's load is issued as soon as head
-//      0's M1 retires, the next unit's head 0 once every M1 has retired
+//      each head's state streams HBM -> shared by TMA (128B swizzle, no
+//      multicast): the next unit's head 0 into its slot once this unit's M1 of
+//      head 0 has retired, head 1 into the R^T region once M2 has read it
 //   C  per v-head: A = strict-anc(beta k.k^T e^{G_i-G_j}) and PD = q.k^T . D;
 //      X = (I + A)^-1 by forward substitution and Z = PD X by backward
 //      substitution of Z (I + A) = PD, on two warps at once -> operand tile
@@ -161,17 +165,17 @@ __device__ __forceinline__ int part_channel(int p, int hk, int Hk, int R) {
   return p == 0 ? hk * kD : (p == 1 ? KD + hk * kD : 2 * KD + (hk * R + p - 2) * kD);
 }
 
-// Per-unit masks and gates of unit u into buffer buf, by warps 13-15 (warp
-// 15: ancestor masks and conv taps; warps 13, 14: gates of v-head warp - 13).
-// Every global load is issued before any of their values is used.
+// Per-unit masks and gates of unit u into buffer buf, by three warps (role 2:
+// ancestor masks and conv taps; roles 0, 1: gates of v-head role).  Every
+// global load is issued before any of their values is used.
 template <int R, bool CONV>
 __device__ __forceinline__ void prep_unit(const dft_gdn_args& a, const dft_gdn_conv_args& cv, Small& sm,
-                                          int32_t* status, int u, int buf, int warp, int lane) {
+                                          int32_t* status, int u, int buf, int role, int lane) {
   const int N = a.N, Hk = a.Hk;
   const int b = u / Hk, hk = u % Hk;
   const int n = lane;
-  const int hl = warp - 13, h = hk * R + hl;
-  const bool gate = warp < 15 && hl < R && n < N;
+  const int hl = role, h = hk * R + hl;
+  const bool gate = role < 2 && hl < R && n < N;
   // gate inputs (raw bits) and conv columns first
   uint32_t ra = 0, rb = 0, rd = 0;
   float dec = 0.f;
@@ -183,13 +187,13 @@ __device__ __forceinline__ void prep_unit(const dft_gdn_args& a, const dft_gdn_c
     dec = a.neg_exp_A ? __ldg(a.neg_exp_A + h) : -expf(__ldg(a.A_log + h));
   }
   int64_t c4[4] = {0, 0, 0, 0};
-  if (CONV && warp == 15 && n < N) {
+  if (CONV && role == 2 && n < N) {
     const int64_t* ci = cv.cidx + ((int64_t)b * N + n) * 4;
 #pragma unroll
     for (int j = 0; j < 4; ++j) c4[j] = __ldg(reinterpret_cast<const long long*>(ci) + j);
   }
   const uint32_t m = anc_mask_warp(a.anc, b, N, lane);
-  if (warp == 15) {
+  if (role == 2) {
     sm.anc[buf][n] = m;
     if (CONV) {
       uint32_t packed = 0;
@@ -354,21 +358,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   };
   if (conv_thr && (int)blockIdx.x < units) load_conv(blockIdx.x);
-  if (warp >= 13 && (int)blockIdx.x < units) prep_unit<R, CONV>(a, ta.cv, sm, status, blockIdx.x, 0, warp, lane);
+  if (warp >= 13 && (int)blockIdx.x < units) prep_unit<R, CONV>(a, ta.cv, sm, status, blockIdx.x, 0, warp - 13, lane);
 
-  int it = 0;
-  for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
-    const int b = u / Hk, hk = u % Hk;
-    const uint32_t ph = it & 1;
-    const int cb = it & 1;   // this unit's buffer of per-unit inputs
-    // ------------------------------------------------ F1: the activation tile
-    if (!mbar_wait(bar_x, ph)) atomicExch(&sm.abort, 1);
-    if (ctl) ++x_used;
-    __syncwarp();
-    __syncthreads();
-    if (sm.abort) break;
-    // ------------------------------------------------ F2: tree conv in place (fc1_conv.py:8-27)
-    if (conv_thr) {
+  // F2, tree conv in place (fc1_conv.py:8-27) of unit cu from taps buffer cbuf,
+  // by the conv threads (warps 0 .. 2 + R - 1): the first unit's at the top of
+  // the loop, every later unit's at the end of the previous unit, alongside
+  // that unit's M2 and E2 (the activation tile is free once E1 has read v)
+  auto do_conv = [&](int cu, int cbuf) {
       const f32x2 w0 = pk2(__uint_as_float(pw.x << 16), __uint_as_float(pw.z << 16));
       const f32x2 w1 = pk2(__uint_as_float(pw.x & 0xFFFF0000u), __uint_as_float(pw.z & 0xFFFF0000u));
       const f32x2 w2 = pk2(__uint_as_float(pw.y << 16), __uint_as_float(pw.w << 16));
@@ -379,8 +375,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 3; ++j) st_s32(colp + j * kRowB, (uint32_t)ps[2 * j] | ((uint32_t)ps[2 * j + 1] << 16));
       {
-        const int nu = u + gridDim.x;
-        if (nu < units) load_conv(nu);   // in flight until the next unit's conv
+        const int nu = cu + gridDim.x;
+        if (nu < units) load_conv(nu);   // in flight until that unit's conv
       }
       // one node: products and sums rounded in order j = 0..3 (fc1_conv.py:20),
       // bias, SiLU, rounded to bf16
@@ -400,23 +396,40 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (; n >= 3; n -= 4) {
         // all four nodes read their taps before any writes (a lower one may be a tap)
-        const f32x2 ya = node(sm.taps[cb][n], n);
-        const f32x2 yb = node(sm.taps[cb][n - 1], n - 1);
-        const f32x2 yc = node(sm.taps[cb][n - 2], n - 2);
-        const f32x2 yd = node(sm.taps[cb][n - 3], n - 3);
+        const f32x2 ya = node(sm.taps[cbuf][n], n);
+        const f32x2 yb = node(sm.taps[cbuf][n - 1], n - 1);
+        const f32x2 yc = node(sm.taps[cbuf][n - 2], n - 2);
+        const f32x2 yd = node(sm.taps[cbuf][n - 3], n - 3);
         st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(ya));
         st_s32(colp + (2 + n) * kRowB, f32x2_to_bf16x2(yb));
         st_s32(colp + (1 + n) * kRowB, f32x2_to_bf16x2(yc));
         st_s32(colp + n * kRowB, f32x2_to_bf16x2(yd));
       }
 #pragma unroll 1
-      for (; n >= 0; --n) st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(node(sm.taps[cb][n], n)));
+      for (; n >= 0; --n) st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(node(sm.taps[cbuf][n], n)));
+  };
+
+  int it = 0;
+  for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+    const int b = u / Hk, hk = u % Hk;
+    const uint32_t ph = it & 1;
+    const int cb = it & 1;   // this unit's buffer of per-unit inputs
+    // ------------------------------------------------ F1: the activation tile
+    if (it == 0) {
+      if (!mbar_wait(bar_x, ph)) atomicExch(&sm.abort, 1);
+      if (ctl) ++x_used;
+      __syncwarp();
+      __syncthreads();
+      if (sm.abort) break;
+      if (conv_thr) do_conv(u, cb);
+    } else if (!CONV && ctl) {
+      // the tile (y, no conv) streamed by TMA since the previous unit's E1
+      if (!mbar_wait(bar_x, ph)) atomicExch(&sm.abort, 1);
+      ++x_used;
     }
-    if (warp >= 13) {
-      const int nu = u + gridDim.x;
-      if (nu < units) prep_unit<R, CONV>(a, ta.cv, sm, status, nu, cb ^ 1, warp, lane);
-    }
+    __syncwarp();
     __syncthreads();
+    if (sm.abort) break;
     // ------------------------------------------------ F3: norms, [k; q] operand, k_hat rows
     {
       // warp w: nodes w and w + 16, q and k, as four independent chains
@@ -636,6 +649,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();   // the control warp reconverges before its E1 (warp-collective TMEM loads)
     }
+    // ------------------------------------------------ the next unit's masks and gates (warps 0, 1, 4)
+    if (warp == 0 || warp == 1 || warp == 4) {
+      const int nu = u + gridDim.x;
+      if (nu < units) prep_unit<R, CONV>(a, ta.cv, sm, status, nu, cb ^ 1, warp == 4 ? 2 : warp, lane);
+    }
     // ------------------------------------------------ E1 (warps 8-15), alongside the X / Z solves
     if (warp >= 8 && ((warp - 8) >> 2) < R) {
       // E1: R = beta (v - e^G (k S0)) by the four warps owning head hh's TMEM lanes
@@ -677,9 +695,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (sm.abort) break;
     if (ctl_warp) {
       if (lane == 0) {
-        // the tile is consumed: request the next unit's
+        // the tile is consumed: request the next unit's (with the fused conv the
+        // conv threads gather it themselves at the end of this unit)
         const int nu = u + gridDim.x;
-        if (nu < units) {
+        if (!CONV && nu < units) {
           issue_act(nu);
           ++x_issued;
         }
@@ -701,18 +720,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();   // the control warp reconverges before the next CTA barrier
     }
-    if (R == 2 && warp == 0) {
-      if (lane == 0) {
-        // once M2 has read R^T, the region takes the next unit's head-1 state
-        const int nu = u + gridDim.x;
-        if (nu < units) {
-          if (!mbar_wait(bar_m2[R - 1], ph)) atomicExch(&sm.abort, 1);
-          issue_state(nu, 1);
-          ++sm.s1_issued;
-        }
-      }
-      __syncwarp();
-    }
     // ------------------------------------------------ E2: vn and o = e^G (q S0) + Z R
     // thread v holds column v: for each node row a warp writes 32 consecutive
     // elements (128 bytes of vn, 64 bytes of o); no shared-memory staging, so
@@ -720,6 +727,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp >= 8 && ((warp - 8) >> 2) < R) {
       const int hh = (warp - 8) >> 2;
       if (!mbar_wait(bar_m2[hh], ph)) atomicExch(&sm.abort, 1);
+      if (R == 2 && ctl) {
+        // M2 has read R^T: the region takes the next unit's head-1 state
+        const int nu = u + gridDim.x;
+        if (nu < units) {
+          issue_state(nu, 1);
+          ++sm.s1_issued;
+        }
+      }
       tc_fence_after();
       const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
       const int h = hk * R + hh, v = tid & 127;
@@ -744,6 +759,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      }
+    }
+    // ------------------------------------------------ the next unit's tile and conv (warps 0 .. 2 + R - 1)
+    // The conv threads gather the next unit's pre-conv rows with 16-byte
+    // cp.async (a DRAM round trip, not queued behind shared-memory traffic as
+    // a TMA write is here), then convert them while warps 8+ run M2 and E2.
+    if (conv_thr) {
+      const int nu = u + gridDim.x;
+      if (nu < units) {
+        constexpr int kConvThreads = 64 * (2 + R);
+        const int nb = nu / Hk, nhk = nu % Hk;
+        const unsigned char* xb = static_cast<const unsigned char*>(ta.cv.x) + (int64_t)nb * ta.cv.x_sb * 2;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int id = tid + kConvThreads * i;
+          const int p = id >> 9, row = (id >> 4) & 31, c16 = id & 15;
+          const bool in = row < N;
+          const unsigned char* src =
+              xb + ((int64_t)(in ? row : 0) * ta.cv.x_sn + part_channel(p, nhk, Hk, R)) * 2 + c16 * 16;
+          cp_async16(sbase + OFF_ACT + p * kPartB + (kOff + row) * kRowB + c16 * 16, src, in ? 16u : 0u, once);
+        }
+        cp_async_wait_all();
+        named_bar(1, kConvThreads);
+        do_conv(nu, cb ^ 1);
       }
     }
     tc_fence_before();
