@@ -318,10 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   int s_issued = 0, s_used = 0, s1_used = 0, x_issued = 0, x_used = 0;
   if (ctl_warp) {
     if (lane == 0 && (int)blockIdx.x < units) {
-      issue_act(blockIdx.x);
+      if (!CONV) {
+        issue_act(blockIdx.x);   // with the fused conv the conv threads gather it
+        x_issued = 1;
+      }
       issue_state(blockIdx.x, 0);
       s_issued = 1;
-      x_issued = 1;
       if (R == 2) {
         issue_state(blockIdx.x, 1);
         sm.s1_issued = 1;
@@ -409,6 +411,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (; n >= 0; --n) st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(node(sm.taps[cbuf][n], n)));
   };
 
+  // the pre-conv rows of unit gu into the activation tile, by the conv threads
+  // (16-byte cp.async, rows >= N zero-filled), complete for all of them on return
+  auto gather_tile = [&](int gu) {
+    constexpr int kConvThreads = 64 * (2 + R);
+    const int nb = gu / Hk, nhk = gu % Hk;
+    const unsigned char* xb = static_cast<const unsigned char*>(ta.cv.x) + (int64_t)nb * ta.cv.x_sb * 2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int id = tid + kConvThreads * i;
+      const int p = id >> 9, row = (id >> 4) & 31, c16 = id & 15;
+      const bool in = row < N;
+      const unsigned char* src =
+          xb + ((int64_t)(in ? row : 0) * ta.cv.x_sn + part_channel(p, nhk, Hk, R)) * 2 + c16 * 16;
+      cp_async16(sbase + OFF_ACT + p * kPartB + (kOff + row) * kRowB + c16 * 16, src, in ? 16u : 0u, once);
+    }
+    cp_async_wait_all();
+    named_bar(1, kConvThreads);
+  };
+
   int it = 0;
   for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
     const int b = u / Hk, hk = u % Hk;
@@ -416,12 +437,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int cb = it & 1;   // this unit's buffer of per-unit inputs
     // ------------------------------------------------ F1: the activation tile
     if (it == 0) {
-      if (!mbar_wait(bar_x, ph)) atomicExch(&sm.abort, 1);
-      if (ctl) ++x_used;
+      if (!CONV) {
+        if (!mbar_wait(bar_x, ph)) atomicExch(&sm.abort, 1);
+        if (ctl) ++x_used;
+      }
       __syncwarp();
       __syncthreads();
       if (sm.abort) break;
-      if (conv_thr) do_conv(u, cb);
+      if (conv_thr) {
+        gather_tile(u);
+        do_conv(u, cb);
+      }
     } else if (!CONV && ctl) {
       // the tile (y, no conv) streamed by TMA since the previous unit's E1
       if (!mbar_wait(bar_x, ph)) atomicExch(&sm.abort, 1);
@@ -768,20 +794,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (conv_thr) {
       const int nu = u + gridDim.x;
       if (nu < units) {
-        constexpr int kConvThreads = 64 * (2 + R);
-        const int nb = nu / Hk, nhk = nu % Hk;
-        const unsigned char* xb = static_cast<const unsigned char*>(ta.cv.x) + (int64_t)nb * ta.cv.x_sb * 2;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int id = tid + kConvThreads * i;
-          const int p = id >> 9, row = (id >> 4) & 31, c16 = id & 15;
-          const bool in = row < N;
-          const unsigned char* src =
-              xb + ((int64_t)(in ? row : 0) * ta.cv.x_sn + part_channel(p, nhk, Hk, R)) * 2 + c16 * 16;
-          cp_async16(sbase + OFF_ACT + p * kPartB + (kOff + row) * kRowB + c16 * 16, src, in ? 16u : 0u, once);
-        }
-        cp_async_wait_all();
-        named_bar(1, kConvThreads);
+        gather_tile(nu);
         do_conv(nu, cb ^ 1);
       }
     }
