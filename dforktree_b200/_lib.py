@@ -101,7 +101,7 @@ class GdnArgs(C.Structure):
                 ("aux_k", vp), ("aux_k_per_v", i32), ("ak_sb", i64), ("ak_sh", i64), ("ak_sn", i64),
                 ("aux_vn", vp), ("av_sb", i64), ("av_sh", i64), ("av_sn", i64),
                 ("aux_g", vp), ("ag_sb", i64), ("ag_sh", i64),
-                ("conv", C.POINTER(GdnConvArgs)), ("force_simt", i32)]
+                ("conv", C.POINTER(GdnConvArgs)), ("force_simt", i32), ("overlap_prev", i32)]
 
 
 class CommitArgs(C.Structure):

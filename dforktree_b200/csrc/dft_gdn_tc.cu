@@ -316,12 +316,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   // control-thread bookkeeping for the drain on timeout
   int s_issued = 0, s_used = 0, s1_used = 0, x_issued = 0, x_used = 0;
+  // Up to the grid-dependency wait below, the CTA reads only what the previous
+  // kernel in the stream does not write (dft_gdn_args.overlap_prev): states,
+  // conv state and weights, ancestor masks, conv columns.  Launched without
+  // the programmatic attribute, the wait returns at once.
   if (ctl_warp) {
     if (lane == 0 && (int)blockIdx.x < units) {
-      if (!CONV) {
-        issue_act(blockIdx.x);   // with the fused conv the conv threads gather it
-        x_issued = 1;
-      }
       issue_state(blockIdx.x, 0);
       s_issued = 1;
       if (R == 2) {
@@ -360,7 +360,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   };
   if (conv_thr && (int)blockIdx.x < units) load_conv(blockIdx.x);
-  if (warp >= 13 && (int)blockIdx.x < units) prep_unit<R, CONV>(a, ta.cv, sm, status, blockIdx.x, 0, warp - 13, lane);
+  if (warp == 15 && (int)blockIdx.x < units) prep_unit<R, CONV>(a, ta.cv, sm, status, blockIdx.x, 0, 2, lane);
+  // activations (x or y, a, bg) and every global write come after the
+  // previous kernel has completed; the next launch may then be scheduled (its
+  // CTAs take an SM as soon as this kernel's CTA there exits)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (ctl && !CONV && (int)blockIdx.x < units) {
+    issue_act(blockIdx.x);   // with the fused conv the conv threads gather it
+    x_issued = 1;
+  }
+  if ((warp == 13 || warp == 14) && (int)blockIdx.x < units)
+    prep_unit<R, CONV>(a, ta.cv, sm, status, blockIdx.x, 0, warp - 13, lane);
 
   // F2, tree conv in place (fc1_conv.py:8-27) of unit cu from taps buffer cbuf,
   // by the conv threads (warps 0 .. 2 + R - 1): the first unit's at the top of
@@ -936,7 +947,19 @@ int dft_gdn_tc_launch(const dft_gdn_args* a, int32_t* status, cudaStream_t st) {
   auto go = [&](auto kernel) -> int {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return DFT_ERR_CUDA;
-    kernel<<<grid, kThreads, smem, st>>>(pool_map, act_map, ta, status);
+    // overlap_prev: programmatic dependent launch (the kernel's own
+    // griddepcontrol.wait orders its activation reads and its writes)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = a->overlap_prev ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kernel, pool_map, act_map, ta, status) != cudaSuccess) return DFT_ERR_CUDA;
     return DFT_OK;
   };
   int rc;

@@ -88,12 +88,16 @@ class DraftTreeCycle:
                       status=self.status)
 
     def verify_layer(self, l, x, a, b):
-        """Tree conv fused into the GDN tree verify of layer l (one launch)."""
+        """Tree conv fused into the GDN tree verify of layer l (one launch).
+        From layer 1 on the launch overlaps the previous layer's verify (which
+        writes none of this layer's states, conv state, weights or tree); layer
+        0 follows the tree build."""
         c = self.cfg
         conv = dict(x=x, conv_state=self.conv_state[l], weight=self.conv_w[l], cidx=self.tree["cidx"])
         K.gdn_tree_verify(None, a, b, None, self.dt_bias[l], self.tree["anc"], self.pool[l], c.Hk, c.Hv, c.D, c.D,
                           neg_exp_A=self.neg_exp_A[l], o=self.o, aux_k=self.aux_k[l], aux_vn=self.aux_vn[l],
-                          aux_g=self.aux_g[l], aux_k_per_v=False, status=self.status, conv=conv)
+                          aux_g=self.aux_g[l], aux_k_per_v=False, status=self.status, conv=conv,
+                          overlap_prev=l > 0)
 
     def verify_layer_unfused(self, l, x, a, b):
         """Separate tree conv launch, then the verify (the plugin's hook order)."""

@@ -319,7 +319,7 @@ def conv_commit(x, conv_state, cidx, last, slots=None, status=None):
 # -------------------------------------------------------- GDN tree verify --
 def gdn_tree_verify(y, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk=128, Dv=128, state_slots=None, scale=None,
                     neg_exp_A=None, o=None, aux_k=None, aux_vn=None, aux_g=None, aux_k_per_v=True, status=None,
-                    pool_strides=None, pool_nslots=None, conv=None, force_simt=False):
+                    pool_strides=None, pool_nslots=None, conv=None, force_simt=False, overlap_prev=False):
     """Batched tree GDN verify.
 
     y [B, N, 2*Hk*Dk + Hv*Dv] (last stride 1) -- or None with conv = dict(x=[B, N, C]
@@ -330,6 +330,11 @@ def gdn_tree_verify(y, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk=128, Dv=128, 
     element strides overrides pool.stride() for views torch cannot express);
     anc [B, N, N] f32; o [B, N, Hv, Dv].
     aux_k [B, Hv or Hk, N, Dk], aux_vn [B, Hv, N, Dv], aux_g [B, Hv, N].
+    overlap_prev: programmatic dependent launch -- the caller guarantees that
+    the kernel queued just before this call writes none of pool, anc, the conv
+    state / weights / columns and the slot maps (the previous layer's verify
+    does not); dropped when an argument needs a conversion here (that copy
+    would be the kernel just before).
     """
     lib = L.lib()
     ref = y if y is not None else conv["x"]
@@ -338,7 +343,9 @@ def gdn_tree_verify(y, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk=128, Dv=128, 
     if o is None:
         o = torch.empty(B, N, Hv, Dv, dtype=ref.dtype, device=ref.device)
     assert o.stride(3) == 1
+    anc_in = anc
     anc = anc.reshape(B, N, N).to(torch.float32).contiguous()
+    converted = anc.data_ptr() != anc_in.data_ptr()
     if scale is None:
         scale = Dk ** -0.5
     A_log_f = None if A_log is None else A_log.to(torch.float32).contiguous()
@@ -357,6 +364,10 @@ def gdn_tree_verify(y, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk=128, Dv=128, 
         cidx = conv["cidx"].reshape(B, N, 4).to(torch.int64).contiguous()
         cslots = conv.get("conv_slots")
         cslots = None if cslots is None else cslots.to(torch.int64).contiguous()
+        converted = converted or w.data_ptr() != conv["weight"].data_ptr() or \
+            cidx.data_ptr() != conv["cidx"].data_ptr() or \
+            (bias is not None and bias.data_ptr() != conv["bias"].data_ptr()) or \
+            (cslots is not None and cslots.data_ptr() != conv["conv_slots"].data_ptr())
         cv = L.GdnConvArgs(x=x.data_ptr(), x_dtype=L.dtype_code(x), x_sb=x.stride(0), x_sn=x.stride(1),
                            conv_state=cs.data_ptr(), cs_dtype=L.dtype_code(cs), cs_ss=cs.stride(0),
                            cs_sc=cs.stride(1), cs_st=cs.stride(2), conv_slots=L.ptr(cslots), weight=w.data_ptr(),
@@ -379,7 +390,8 @@ def gdn_tree_verify(y, a, b, A_log, dt_bias, anc, pool, Hk, Hv, Dk=128, Dv=128, 
                      av_sn=aux_vn.stride(2) if aux_vn is not None else 0,
                      aux_g=L.ptr(aux_g), ag_sb=aux_g.stride(0) if aux_g is not None else 0,
                      ag_sh=aux_g.stride(1) if aux_g is not None else 0,
-                     conv=C.pointer(cv) if cv is not None else None, force_simt=int(bool(force_simt)))
+                     conv=C.pointer(cv) if cv is not None else None, force_simt=int(bool(force_simt)),
+                     overlap_prev=int(bool(overlap_prev) and not converted))
     keep = (anc, A_log_f, neg, dtb, keep_cv, cv)
     rc = lib.dft_gdn_tree_verify(C.byref(args), _status_ptr(status), L.stream_handle())
     del keep

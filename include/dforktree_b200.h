@@ -272,6 +272,16 @@ typedef struct {
   float* aux_g; int64_t ag_sb, ag_sh;
   const dft_gdn_conv_args* conv;  /* NULL: read y                           */
   int32_t force_simt;             /* 1: CUDA-core path even where the tcgen05 path applies */
+  /* 1: programmatic dependent launch (tcgen05 path).  The launch may start
+   * while the previous kernel in the stream is still running: its set-up,
+   * state / conv-state / conv-weight loads and the ancestor masks and conv
+   * columns (pool, state_slots, conv_state, conv_slots, weight, bias, anc,
+   * cidx) are read before it waits for that kernel; everything else (x or y,
+   * a, bg, dt_bias, A_log / neg_exp_A) and every write come after.  The
+   * caller guarantees that the previous kernel writes none of the former
+   * (e.g. it is the previous layer's verify, or the layer's input
+   * projection).  0: an ordinary launch. */
+  int32_t overlap_prev;
 } dft_gdn_args;
 DFT_API int dft_gdn_tree_verify(const dft_gdn_args* a, int32_t* dev_status, void* stream);
 

@@ -83,7 +83,7 @@ int main(void) {
   F(dft_tree_attn_args, max_kv_len) F(dft_tree_attn_args, o) F(dft_tree_attn_args, o_sh)
   F(dft_table_desc, max_load) F(dft_table_desc, n4c) F(dft_build_params, lam_p)
   F(dft_conv_args, iw_slots) F(dft_conv_args, y_dtype) F(dft_gdn_args, ag_sh) F(dft_gdn_args, pool)
-  F(dft_gdn_args, aux_k_per_v) F(dft_commit_args, ends) F(dft_commit_args, aux_k_per_v) F(dft_commit_args, so_sk)
+  F(dft_gdn_args, aux_k_per_v) F(dft_gdn_args, overlap_prev) F(dft_commit_args, ends) F(dft_commit_args, aux_k_per_v) F(dft_commit_args, so_sk)
   return 0;
 }
 """

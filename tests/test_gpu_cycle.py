@@ -127,6 +127,54 @@ def test_tensor_core_verify_many_units_per_cta(N):
     np.testing.assert_allclose(_np(tc[3]), _np(si[3]), rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("conv", [True, False])
+def test_overlapped_layer_launches_equal_ordinary_launches(conv):
+    """Programmatic dependent launch (overlap_prev): layers launched back to
+    back, each overlapping the previous layer's verify, give bit-identical
+    outputs to ordinary launches -- including a shared o buffer (each layer's
+    writes wait for the previous layer) and the y-input path whose activation
+    TMA is issued after the wait."""
+    from dforktree_b200 import kernels as K
+    Hk, Hv, L, B = 16, 32, 4, 40
+    layers = [_layer_inputs(B, 32, Hk, Hv, 128, seed=300 + l, dtype=torch.bfloat16) for l in range(L)]
+    for d in layers[1:]:   # one tree per cycle, as in the plugin
+        d["anc"], d["cidx"] = layers[0]["anc"], layers[0]["cidx"]
+    ys = [None if conv else K.tree_conv(d["x"], d["conv_state"], d["weight"], None, d["cidx"]) for d in layers]
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+
+    def run(overlap, o_shared=None):
+        # every buffer allocated up front: nothing is queued between the launches
+        outs = [(o_shared if o_shared is not None else torch.empty(B, 32, Hv, 128, dtype=torch.bfloat16, device=DEV),
+                 torch.zeros(B, Hk, 32, 128, device=DEV), torch.zeros(B, Hv, 32, 128, device=DEV),
+                 torch.zeros(B, Hv, 32, device=DEV)) for _ in layers]
+        cvs = [dict(x=d["x"], conv_state=d["conv_state"], weight=d["weight"], cidx=d["cidx"]) if conv else None
+               for d in layers]
+        torch.cuda.synchronize()
+        for l, d in enumerate(layers):
+            o, ak, av, ag = outs[l]
+            K.gdn_tree_verify(ys[l], d["a"], d["b"], d["A_log"], d["dtb"], d["anc"], d["pool"], Hk, Hv, aux_k=ak,
+                              aux_vn=av, aux_g=ag, aux_k_per_v=False, conv=cvs[l], status=st, o=o,
+                              overlap_prev=overlap and l > 0)
+            if not overlap:
+                torch.cuda.synchronize()
+        return outs
+
+    ref = run(False)
+    torch.cuda.synchronize()
+    got = run(True)
+    torch.cuda.synchronize()
+    o_shared = torch.empty(B, 32, Hv, 128, dtype=torch.bfloat16, device=DEV)
+    shared = run(True, o_shared)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    for l in range(L):
+        for r, g_ in zip(ref[l], got[l]):
+            assert torch.equal(r, g_), l
+        for r, g_ in zip(ref[l][1:], shared[l][1:]):
+            assert torch.equal(r, g_), l
+    assert torch.equal(o_shared, ref[-1][0])
+
+
 def test_cycle_step_matches_oracle_chain():
     """One batched cycle (B=4, 2 GDN layers, V=2048) request by request."""
     from dforktree_b200 import kernels as K
