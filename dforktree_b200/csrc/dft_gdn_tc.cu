@@ -16,20 +16,20 @@
 //      from last to first (a node's taps are its ancestors, lower indices);
 //      then one warp per node pair: L2 norms of q / k, the swizzled tf32
 //      operand [k; q] and the fp32 k_hat rows (stored to aux_k).  The next
-//      unit's gates and ancestor masks are computed by warps 0, 1, 4 during
-//      this unit's X / Z solves
+//      unit's gates and ancestor masks are computed by warps 10, 11, 14
+//      during this unit's C1 (their loads ahead of the next states' copies)
 //   M0 tcgen05 MMA  D0 = [k; q] k^T          -> k.k^T and q.k^T  (TMEM)
-//   M1 tcgen05 MMA  D1_h = S0_h [k; q]^T     -> (k S0)^T, (q S0)^T per v-head;
-//      each head's state streams HBM -> shared by TMA (128B swizzle, no
-//      multicast): the next unit's head 0 into its slot once this unit's M1 of
-//      head 0 has retired, head 1 into the R^T region once M2 has read it
+//   M1 tcgen05 MMA  D1_h = S0_h [k; q]^T     -> (k S0)^T, (q S0)^T per v-head,
+//      head 1's issued right behind head 0's; each head's state streams HBM ->
+//      its own shared slot by TMA (128B swizzle, no multicast), the next
+//      unit's once this unit's M1 of that head has retired (a whole unit ahead)
 //   C  per v-head: A = strict-anc(beta k.k^T e^{G_i-G_j}) and PD = q.k^T . D;
 //      X = (I + A)^-1 by forward substitution and Z = PD X by backward
 //      substitution of Z (I + A) = PD, on two warps at once -> operand tile
 //      [X; Z] (3xTF32 hi / lo), written over [k; q] once every M1 has retired
-//   E1 R = beta (v - e^G (k S0)) by the thread owning TMEM lane v -> R^T tile
-//      (alongside C's solves)
-//   M2 tcgen05 MMA  D2_h = R^T [X; Z]^T (3xTF32) -> vn^T and (Z R)^T
+//   E1 R = beta (v - e^G (k S0)) by the thread owning TMEM lane v -> row v of
+//      R^T (hi / lo) stored back to TMEM lane v (alongside C's solves)
+//   M2 tcgen05 MMA  D2_h = R^T [X; Z]^T (3xTF32, A from TMEM) -> vn^T, (Z R)^T
 //   E2 o = e^G (q S0) + Z R and vn from TMEM straight to global memory (per
 //      node row, one warp writes 32 consecutive elements)
 // The state is read once, at tensor-core rate, and everything else stays on
@@ -53,15 +53,15 @@ constexpr int kNP = 32;            // nodes per tree, padded
 constexpr int kThreads = 512;
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns: [0,32) k.k^T (lanes 0-31) | q.k^T (lanes 32-63); v-head h:
-// [32 + 64h, 96 + 64h) (k S0)^T | (q S0)^T and [160 + 64h, 224 + 64h) vn^T | (Z R)^T
-constexpr uint32_t COL_M0 = 0, COL_M1 = 32, COL_M2 = 160;
+// [32 + 64h, 96 + 64h) (k S0)^T | (q S0)^T, [160 + 64h, 224 + 64h) vn^T | (Z R)^T
+// and [288 + 64h, 352 + 64h) R^T hi | lo (M2's A operand, lane v = row v)
+constexpr uint32_t COL_M0 = 0, COL_M1 = 32, COL_M2 = 160, COL_RT = 288;
 
 // shared memory map (from a 1024-byte aligned base)
 constexpr uint32_t kS0Bytes = 64 * 1024;   // one state tile: 4 K-blocks [128 x 128 B]
 constexpr uint32_t OFF_S0 = 0;
 constexpr uint32_t OFF_KQ = 64 * 1024;     // [k; q] operand (4 K-blocks [64 x 128 B]); then [X; Z] hi, lo of head h at +16 KB h
-constexpr uint32_t OFF_RT = 96 * 1024;     // head 1's state tile (TMA) until its M1 retires; then head h at
-                                           // +32 KB h: R^T hi, lo (16 KB each) until M2 retires
+constexpr uint32_t OFF_S1 = 96 * 1024;     // head 1's state tile (TMA)
 constexpr uint32_t OFF_U = 160 * 1024;     // head h at +12 KB h: A, PD, A' (4 KB each; A'[p][q] = A[31-q][31-p])
 constexpr uint32_t U_A = 0, U_PD = 4096, U_AT = 8192, kUHead = 12288;
 constexpr uint32_t OFF_SMALL = 184 * 1024;
@@ -293,14 +293,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
 
   const uint64_t once = l2_evict_first();
-  // state of v-head hl of unit u: head 0 into the state slot, head 1 into the
-  // R^T region (free from the end of the previous unit until this unit's M1
-  // of head 1 has retired)
+  // state of v-head hl of unit u into that head's slot (free once the previous
+  // unit's M1 of the head has retired)
   auto issue_state = [&](int u, int hl) {
     const int b = u / Hk, hk = u % Hk;
     const long long s = a.state_slots ? a.state_slots[b] : b;
     const int slot = s < 0 ? 0 : (int)s;
-    const uint32_t bar = hl ? bar_s1 : bar_s, dst = sbase + (hl ? OFF_RT : OFF_S0);
+    const uint32_t bar = hl ? bar_s1 : bar_s, dst = sbase + (hl ? OFF_S1 : OFF_S0);
     mbar_expect_tx(bar, kS0Bytes);
 #pragma unroll
     for (int kb = 0; kb < 4; ++kb) tma_load_4d(dst + kb * 16384, &pool_map, 32 * kb, 0, hk * R + hl, slot, bar, once);
@@ -391,35 +390,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nu = cu + gridDim.x;
         if (nu < units) load_conv(nu);   // in flight until that unit's conv
       }
-      // one node: products and sums rounded in order j = 0..3 (fc1_conv.py:20),
-      // bias, SiLU, rounded to bf16
-      auto node = [&](uint32_t tp, int n) -> f32x2 {
-        const f32x2 x0 = bf16x2_to_f32x2(ld_s32(colp + (int)(tp & 0xFFu) * kRowB));
-        const f32x2 x1 = bf16x2_to_f32x2(ld_s32(colp + (int)((tp >> 8) & 0xFFu) * kRowB));
-        const f32x2 x2 = bf16x2_to_f32x2(ld_s32(colp + (int)((tp >> 16) & 0xFFu) * kRowB));
-        const f32x2 x3 = bf16x2_to_f32x2(ld_s32(colp + (3 + n) * kRowB));
-        f32x2 acc = mul2(x0, w0);
-        acc = add2(acc, mul2(x1, w1));
-        acc = add2(acc, mul2(x2, w2));
-        acc = add2(acc, mul2(x3, w3));
-        if (has_bias) acc = add2(acc, bias2);
-        return silu_hw2(acc);
+      // one node: its three taps and itself (raw bf16 pairs), then products and
+      // sums rounded in order j = 0..3 (fc1_conv.py:20), bias, SiLU, bf16
+      auto load = [&](int n) -> uint4 {
+        const uint32_t tp = sm.taps[cbuf][n];
+        return make_uint4(ld_s32(colp + (int)(tp & 0xFFu) * kRowB), ld_s32(colp + (int)((tp >> 8) & 0xFFu) * kRowB),
+                          ld_s32(colp + (int)((tp >> 16) & 0xFFu) * kRowB), ld_s32(colp + (3 + n) * kRowB));
       };
+      auto node = [&](uint4 in) -> uint32_t {
+        f32x2 acc = mul2(bf16x2_to_f32x2(in.x), w0);
+        acc = add2(acc, mul2(bf16x2_to_f32x2(in.y), w1));
+        acc = add2(acc, mul2(bf16x2_to_f32x2(in.z), w2));
+        acc = add2(acc, mul2(bf16x2_to_f32x2(in.w), w3));
+        if (has_bias) acc = add2(acc, bias2);
+        return f32x2_to_bf16x2(silu_hw2(acc));
+      };
+      // groups of four nodes from the last one down.  A group's inputs are read
+      // before its outputs are written (a lower node of the group may be a tap
+      // of a higher one); the next group's inputs are read before this group's
+      // outputs are written too, which is safe because a node's taps and its
+      // own row all lie below the rows of every node above it.
       int n = N - 1;
-#pragma unroll 1
-      for (; n >= 3; n -= 4) {
-        // all four nodes read their taps before any writes (a lower one may be a tap)
-        const f32x2 ya = node(sm.taps[cbuf][n], n);
-        const f32x2 yb = node(sm.taps[cbuf][n - 1], n - 1);
-        const f32x2 yc = node(sm.taps[cbuf][n - 2], n - 2);
-        const f32x2 yd = node(sm.taps[cbuf][n - 3], n - 3);
-        st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(ya));
-        st_s32(colp + (2 + n) * kRowB, f32x2_to_bf16x2(yb));
-        st_s32(colp + (1 + n) * kRowB, f32x2_to_bf16x2(yc));
-        st_s32(colp + n * kRowB, f32x2_to_bf16x2(yd));
+      uint4 ia, ib, ic, id;
+      if (n >= 3) {
+        ia = load(n);
+        ib = load(n - 1);
+        ic = load(n - 2);
+        id = load(n - 3);
       }
 #pragma unroll 1
-      for (; n >= 0; --n) st_s32(colp + (3 + n) * kRowB, f32x2_to_bf16x2(node(sm.taps[cbuf][n], n)));
+      for (; n >= 3; n -= 4) {
+        uint4 na = ia, nb = ib, nc = ic, nd = id;
+        if (n >= 7) {
+          na = load(n - 4);
+          nb = load(n - 5);
+          nc = load(n - 6);
+          nd = load(n - 7);
+        }
+        const uint32_t ya = node(ia), yb = node(ib), yc = node(ic), yd = node(id);
+        st_s32(colp + (3 + n) * kRowB, ya);
+        st_s32(colp + (2 + n) * kRowB, yb);
+        st_s32(colp + (1 + n) * kRowB, yc);
+        st_s32(colp + n * kRowB, yd);
+        ia = na;
+        ib = nb;
+        ic = nc;
+        id = nd;
+      }
+#pragma unroll 1
+      for (; n >= 0; --n) st_s32(colp + (3 + n) * kRowB, node(load(n)));
   };
 
   // the pre-conv rows of unit gu into the activation tile, by the conv threads
@@ -526,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // ------------------------------------------------ M0, M1 of head 0 (one thread issues)
+    // ------------------------------------------------ M0, M1 of every head (one thread issues)
     if (ctl_warp) {
       if (lane == 0) {
         const uint32_t id0 = idesc_tf32(128, 32), id1 = idesc_tf32(128, 64);
@@ -548,8 +567,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
         }
         mma_commit(bar_m1[0]);
+        if (R == 2) {
+          // head 1's M1 (its state streamed into its own slot since the previous unit's M1)
+          if (!mbar_wait(bar_s1, s1_used & 1)) atomicExch(&sm.abort, 1);
+          ++s1_used;
+          tc_fence_after();
+  #pragma unroll 1
+          for (int kb = 0; kb < 4; ++kb) {
+            const uint64_t da = sw128_desc(sbase + OFF_S1 + kb * 16384);
+            const uint64_t db = sw128_desc(sbase + OFF_KQ + kb * 8192);
+  #pragma unroll
+            for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1 + 64, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
+          }
+          mma_commit(bar_m1[1]);
+        }
       }
       __syncwarp();   // the control warp reconverges before the next CTA barrier
+    }
+    // ------------------------------------------------ the next unit's masks and gates (warps 10, 11, 14)
+    // by warps idle until E1, early in the unit: their loads go out before the
+    // next unit's state copies are queued behind them
+    if (warp == 10 || warp == 11 || warp == 14) {
+      const int nu = u + gridDim.x;
+      if (nu < units) prep_unit<R, CONV>(a, ta.cv, sm, status, nu, cb ^ 1, warp == 14 ? 2 : warp - 10, lane);
     }
     // ------------------------------------------------ C1: A and PD of every head (8 warps)
     // warp w: rows from TMEM lanes 32 (w % 4) (k.k^T for w % 4 == 0, q.k^T for 1),
@@ -585,9 +625,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           at[sq32(28 - j0, 31 - i)] = o.w;
         }
       }
+      // head hh's A / PD / A' are written: release its two solver warps
+      // (named barrier 2 + hh: the four C1 warps of the head arrive, the two
+      // solver warps wait; no other warp waits for C1)
+      asm volatile("bar.arrive %0, %1;" ::"r"(2 + hh), "r"(192) : "memory");
     }
-    __syncthreads();
-    if (sm.abort) break;
     // ------------------------------------------------ X, Z per head (warps 2, 3 / 6, 7)
     // Both are unit lower-triangular solves r_i = init_i - sum_{m < i} L[i][m] r_m,
     // one column / row per lane, in registers:
@@ -599,6 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if ((warp & 3) >= 2 && (warp >> 2) < R) {
       const int hh = warp >> 2;
       const bool zw = warp & 1;
+      named_bar(2 + hh, 192);   // head hh's C1 is done
       const float* L = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + (zw ? U_AT : U_A));
       float r[32];
       if (!zw) {
@@ -661,68 +704,53 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ctl_warp) {
       if (lane == 0) {
-        // head 0's M1 has long retired: its slot takes the next unit's head-0 state
+        // each head's M1 has retired: its slot takes the next unit's state
         const int nu = u + gridDim.x;
         if (nu < units) {
           if (!mbar_wait(bar_m1[0], ph)) atomicExch(&sm.abort, 1);
           issue_state(nu, 0);
           ++s_issued;
-        }
-        if (R == 2) {
-          // head 1's M1 (its state streamed into the R^T region between units)
-          if (!mbar_wait(bar_s1, s1_used & 1)) atomicExch(&sm.abort, 1);
-          ++s1_used;
-          tc_fence_after();
-          const uint32_t id1 = idesc_tf32(128, 64);
-  #pragma unroll 1
-          for (int kb = 0; kb < 4; ++kb) {
-            const uint64_t da = sw128_desc(sbase + OFF_RT + kb * 16384);
-            const uint64_t db = sw128_desc(sbase + OFF_KQ + kb * 8192);
-  #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) mma_tf32(tmem + COL_M1 + 64, da + 2 * ks, db + 2 * ks, id1, (kb | ks) != 0);
+          if (R == 2) {
+            if (!mbar_wait(bar_m1[1], ph)) atomicExch(&sm.abort, 1);
+            issue_state(nu, 1);
+            ++sm.s1_issued;
           }
-          mma_commit(bar_m1[1]);
         }
       }
       __syncwarp();   // the control warp reconverges before its E1 (warp-collective TMEM loads)
     }
-    // ------------------------------------------------ the next unit's masks and gates (warps 0, 1, 4)
-    if (warp == 0 || warp == 1 || warp == 4) {
-      const int nu = u + gridDim.x;
-      if (nu < units) prep_unit<R, CONV>(a, ta.cv, sm, status, nu, cb ^ 1, warp == 4 ? 2 : warp, lane);
-    }
     // ------------------------------------------------ E1 (warps 8-15), alongside the X / Z solves
     if (warp >= 8 && ((warp - 8) >> 2) < R) {
-      // E1: R = beta (v - e^G (k S0)) by the four warps owning head hh's TMEM lanes
+      // E1: R = beta (v - e^G (k S0)) by the four warps owning head hh's TMEM
+      // lanes; row v of R^T (hi / lo tf32 split) goes to TMEM lane v as M2's A
       const int hh = (warp - 8) >> 2;
-      if (!mbar_wait(bar_m1[R - 1], ph)) atomicExch(&sm.abort, 1);   // R^T region free, (k S0) ready
+      if (!mbar_wait(bar_m1[hh], ph)) atomicExch(&sm.abort, 1);   // (k S0) of head hh ready
       tc_fence_after();
+      const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
       float ks_[kNP];
-      tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + COL_M1 + 64 * hh, ks_);
-      unsigned char* rth = smem + OFF_RT + hh * 32768;
-      unsigned char* rtl = rth + 16384;
+      tmem_ld32(tmem + lanes + COL_M1 + 64 * hh, ks_);
       const int v = tid & 127;
       const T* yv = reinterpret_cast<const T*>(act + (2 + hh) * kPartB + kOff * kRowB) + v;
-      // row v of R^T: eight 16-byte chunks, swizzled (chunk c at c ^ (v & 7))
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float4 hi, lo;
-        float* phi = &hi.x;
-        float* plo = &lo.x;
-        const float4 be4 = *reinterpret_cast<const float4*>(&sm.beta[cb][hh][4 * c]);
-        const float4 eg4 = *reinterpret_cast<const float4*>(&sm.eG[cb][hh][4 * c]);
-        const float* be = &be4.x;
-        const float* eg = &eg4.x;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int n = 4 * c + e;
-          const float rr = be[e] * (to_f32(yv[n * kD]) - eg[e] * ks_[n]);
-          phi[e] = tf32_rna(rr);
-          plo[e] = tf32_rna(rr - phi[e]);
+        for (int c = 0; c < 4; ++c) {
+          const float4 be4 = *reinterpret_cast<const float4*>(&sm.beta[cb][hh][16 * half + 4 * c]);
+          const float4 eg4 = *reinterpret_cast<const float4*>(&sm.eG[cb][hh][16 * half + 4 * c]);
+          const float* be = &be4.x;
+          const float* eg = &eg4.x;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int n = 16 * half + 4 * c + e;
+            const float rr = be[e] * (to_f32(yv[n * kD]) - eg[e] * ks_[n]);
+            const float h = tf32_rna(rr);
+            hi[4 * c + e] = __float_as_uint(h);
+            lo[4 * c + e] = __float_as_uint(tf32_rna(rr - h));
+          }
         }
-        const uint32_t off = (uint32_t)(v * 128 + ((c ^ (v & 7)) << 4));
-        *reinterpret_cast<float4*>(rth + off) = hi;
-        *reinterpret_cast<float4*>(rtl + off) = lo;
+        tmem_st16(tmem + lanes + COL_RT + 64 * hh + 16 * half, hi);
+        tmem_st16(tmem + lanes + COL_RT + 64 * hh + 32 + 16 * half, lo);
       }
     }
     fence_async_smem();
@@ -744,14 +772,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll 1
         for (int hh = 0; hh < R; ++hh) {
           const uint32_t dcol = tmem + COL_M2 + 64 * hh;
-          const uint64_t ah = sw128_desc(sbase + OFF_RT + hh * 32768), al = sw128_desc(sbase + OFF_RT + hh * 32768 + 16384);
+          const uint32_t ah = tmem + COL_RT + 64 * hh, al = ah + 32;   // R^T hi / lo in TMEM, 8 columns per K step
           const uint64_t bh = sw128_desc(sbase + OFF_KQ + hh * 16384), bl = sw128_desc(sbase + OFF_KQ + hh * 16384 + 8192);
   #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, ah + 2 * ks, bh + 2 * ks, id2, ks != 0);
+          for (int ks = 0; ks < 4; ++ks) mma_tf32_ts(dcol, ah + 8 * ks, bh + 2 * ks, id2, ks != 0);
   #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, ah + 2 * ks, bl + 2 * ks, id2, 1);
+          for (int ks = 0; ks < 4; ++ks) mma_tf32_ts(dcol, ah + 8 * ks, bl + 2 * ks, id2, 1);
   #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) mma_tf32(dcol, al + 2 * ks, bh + 2 * ks, id2, 1);
+          for (int ks = 0; ks < 4; ++ks) mma_tf32_ts(dcol, al + 8 * ks, bh + 2 * ks, id2, 1);
           mma_commit(bar_m2[hh]);
         }
       }
@@ -759,19 +787,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // ------------------------------------------------ E2: vn and o = e^G (q S0) + Z R
     // thread v holds column v: for each node row a warp writes 32 consecutive
-    // elements (128 bytes of vn, 64 bytes of o); no shared-memory staging, so
-    // the R^T region is free once M2 has read it
+    // elements (128 bytes of vn, 64 bytes of o); no shared-memory staging
     if (warp >= 8 && ((warp - 8) >> 2) < R) {
       const int hh = (warp - 8) >> 2;
       if (!mbar_wait(bar_m2[hh], ph)) atomicExch(&sm.abort, 1);
-      if (R == 2 && ctl) {
-        // M2 has read R^T: the region takes the next unit's head-1 state
-        const int nu = u + gridDim.x;
-        if (nu < units) {
-          issue_state(nu, 1);
-          ++sm.s1_issued;
-        }
-      }
       tc_fence_after();
       const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
       const int h = hk * R + hh, v = tid & 127;

@@ -139,6 +139,15 @@ __device__ __forceinline__ void mma_bf16(uint32_t dtmem, uint64_t adesc, uint64_
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(dtmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+// A from TMEM (lane = row, one tf32 per column along K)
+__device__ __forceinline__ void mma_tf32_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(dtmem),
+      "r"(atmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 // A from TMEM (lane = row, K packed along columns: two bf16 per column)
 __device__ __forceinline__ void mma_bf16_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
