@@ -21,8 +21,8 @@
 //   M0 tcgen05 MMA  D0 = [k; q] k^T          -> k.k^T and q.k^T  (TMEM)
 //   M1 tcgen05 MMA  D1_h = S0_h [k; q]^T     -> (k S0)^T, (q S0)^T per v-head,
 //      head 1's issued right behind head 0's; each head's state streams HBM ->
-//      its own shared slot by TMA (128B swizzle, no multicast), the next
-//      unit's issued with this unit's M2
+//      its own shared slot by TMA (128B swizzle, no multicast): head 0's for
+//      the next unit with this unit's M2, head 1's at the top of its unit
 //   C  per v-head: A = strict-anc(beta k.k^T e^{G_i-G_j}) and PD = q.k^T . D;
 //      X = (I + A)^-1 by forward substitution and Z = PD X by backward
 //      substitution of Z (I + A) = PD, on two warps at once -> operand tile
@@ -468,6 +468,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     __syncthreads();
     if (sm.abort) break;
+    if (R == 2 && ctl && it > 0) {
+      // head 1's state for this unit (its slot is free since the previous
+      // unit's M1): streamed during the norms and C1, whose shared-memory
+      // traffic is light, and needed only at this unit's second M1
+      issue_state(u, 1);
+      ++sm.s1_issued;
+    }
     // ------------------------------------------------ F3: norms, [k; q] operand, k_hat rows
     {
       // warp w: nodes w and w + 16, q and k, as four independent chains
@@ -755,18 +762,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         {
           // every M1 of this unit has retired (the solvers waited for it): the
-          // state slots take the next unit's states.  Issued here rather than
-          // right after M1, so that the copies' shared-memory writes do not
-          // meet the solves' and E1's traffic (measured: 1.5 % faster)
+          // head-0 slot takes the next unit's state.  Issued here rather than
+          // right after M1, so that the copy's shared-memory writes do not meet
+          // the solves' and E1's traffic; head 1's goes out at the top of the
+          // next unit (measured: 1.5 % and 4.5 % faster than both after M1)
           const int nu = u + gridDim.x;
           if (nu < units) {
             if (!mbar_wait(bar_m1[R - 1], ph)) atomicExch(&sm.abort, 1);
             issue_state(nu, 0);
             ++s_issued;
-            if (R == 2) {
-              issue_state(nu, 1);
-              ++sm.s1_issued;
-            }
           }
         }
       }
