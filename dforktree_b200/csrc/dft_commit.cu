@@ -18,7 +18,14 @@ constexpr int kD = 128;
 constexpr int kThreads = 256;
 constexpr int kMaxPath = 64;
 
-__global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args a, int32_t* st) {
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// ahead: the block `ahead` launches later (about two waves) has its path rows
+// of k and vn prefetched into L2 by this block's warp 0, so that its own
+// dependent row loads (after the path set-up) hit L2 instead of DRAM
+__global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args a, int32_t* st, int ahead) {
   extern __shared__ __align__(16) float s_path[];  // [cap][kD] k*w, then [cap][kD] vn
   __shared__ int s_ids[kMaxPath];
   __shared__ float s_w[kMaxPath];
@@ -72,6 +79,27 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args
     // global loads); a ballot compacts the kept nodes in order.
     const float* anc_u = a.anc + ((int64_t)b * a.N + u) * a.N;
     const float an0 = tid < a.N ? anc_u[tid] : 0.f, an1 = tid + 32 < a.N ? anc_u[tid + 32] : 0.f;
+    // the later block's request and path entries (its rows are prefetched below)
+    const int64_t fblk = (int64_t)blockIdx.x + ahead;
+    const bool fut = fblk < (int64_t)gridDim.x;
+    int64_t fid[2] = {-1, -1};
+    const float* fk = nullptr;
+    const float* fv = nullptr;
+    if (fut) {
+      int f = (int)fblk;
+      const int fh = f % a.Hv;
+      f /= a.Hv;
+      const int fb = f % a.B;
+      f /= a.B;
+      const int fl = f % a.L;
+      fk = a.aux_k + (int64_t)fl * a.ak_sl + (int64_t)fb * a.ak_sb + (int64_t)(a.aux_k_per_v ? fh : fh / R) * a.ak_sh;
+      fv = a.aux_vn + (int64_t)fl * a.av_sl + (int64_t)fb * a.av_sb + (int64_t)fh * a.av_sh;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int t = 32 * j + tid;
+        fid[j] = t < a.P ? a.path[(int64_t)fb * a.P + t] : -1;
+      }
+    }
     const float g0 = tid < a.N ? G[tid] : 0.f, g1 = tid + 32 < a.N ? G[tid + 32] : 0.f;
     int64_t pid[2];
 #pragma unroll
@@ -101,6 +129,15 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args
       base += __popc(m);
     }
     if (tid == 0) s_n = base < cap_n ? base : cap_n;
+    if (fut) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        if (fid[j] >= 0 && fid[j] < a.N) {
+          prefetch_l2(fk + fid[j] * a.ak_sn, kD * sizeof(float));
+          prefetch_l2(fv + fid[j] * a.av_sn, kD * sizeof(float));
+        }
+      }
+    }
   }
   __syncthreads();
   const int np = s_n;
@@ -168,7 +205,17 @@ extern "C" int dft_gdn_commit(const dft_commit_args* a, int32_t* dev_status, voi
   if (sm > 48 * 1024 &&
       cudaFuncSetAttribute(gdn_commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
     return DFT_ERR_CUDA;
-  gdn_commit_kernel<<<(unsigned)blocks, kThreads, sm, reinterpret_cast<cudaStream_t>(stream)>>>(*a, dev_status);
+  // the L2 prefetch needs 16-byte aligned rows
+  const bool rows16 = ((uintptr_t)a->aux_k % 16 == 0) && ((uintptr_t)a->aux_vn % 16 == 0) && a->ak_sl % 4 == 0 &&
+                      a->ak_sb % 4 == 0 && a->ak_sh % 4 == 0 && a->ak_sn % 4 == 0 && a->av_sl % 4 == 0 &&
+                      a->av_sb % 4 == 0 && a->av_sh % 4 == 0 && a->av_sn % 4 == 0;
+  int ahead = 0x7fffffff;
+  if (rows16) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    ahead = 4 * sms;   // two CTAs per SM, two waves ahead
+  }
+  gdn_commit_kernel<<<(unsigned)blocks, kThreads, sm, reinterpret_cast<cudaStream_t>(stream)>>>(*a, dev_status, ahead);
   DFT_LAUNCH_CHECK();
   return DFT_OK;
 }
