@@ -296,21 +296,9 @@ def run_ours(args, rank, world, local_rank):
             one_step()
         torch.cuda.synchronize()
         return None
-    # per-stage events on a separate pass of K steps (same work)
     mk = lambda: torch.cuda.Event(enable_timing=True)
-    stage = {"score_build": 0.0, "conv_verify": 0.0, "accept": 0.0, "commit": 0.0}
-    evs = []
-    for _ in range(args.steps):
-        ev = {k: mk() for k in ("sb0", "sb1", "v1", "c0", "c1")}
-        one_step(ev)
-        evs.append(ev)
-    torch.cuda.synchronize()
-    for ev in evs:
-        stage["score_build"] += ev["sb0"].elapsed_time(ev["sb1"])
-        stage["conv_verify"] += ev["sb1"].elapsed_time(ev["v1"])
-        stage["accept"] += ev["v1"].elapsed_time(ev["c0"])
-        stage["commit"] += ev["c0"].elapsed_time(ev["c1"])
-    # per-launch duration of the fused conv + GDN verify (the dominant kernel)
+    # each verify launch alone (events around every launch: no overlap with the
+    # previous layer's launch), reported beside the in-cycle average
     verify_ms = 0.0
     pairs = []
     for _ in range(args.steps):
@@ -333,12 +321,21 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize()
     t0, t1 = mk(), mk()
+    # stage markers inside the timed steps (events between stages: the work and
+    # the launch order are those of DraftTreeCycle.step)
+    evs = [{k: mk() for k in ("sb0", "sb1", "v1", "c0", "c1")} for _ in range(args.steps)]
     with ClockSampler(local_rank) as clk:
         t0.record(stream)
-        for _ in range(args.steps):
-            one_step()
+        for ev in evs:
+            one_step(ev)
         t1.record(stream)
         torch.cuda.synchronize()
+    stage = {"score_build": 0.0, "conv_verify": 0.0, "accept": 0.0, "commit": 0.0}
+    for ev in evs:
+        stage["score_build"] += ev["sb0"].elapsed_time(ev["sb1"])
+        stage["conv_verify"] += ev["sb1"].elapsed_time(ev["v1"])
+        stage["accept"] += ev["v1"].elapsed_time(ev["c0"])
+        stage["commit"] += ev["c0"].elapsed_time(ev["c1"])
     if world > 1:
         dist.barrier()
     ms = t0.elapsed_time(t1)
@@ -398,7 +395,10 @@ def run_ours(args, rank, world, local_rank):
     if rank != 0:
         return None
     hbm, tflops, peak_kind = _peaks()
-    verify_launch_ms = verify_ms / max(n_verify, 1)
+    # the dominant kernel's average launch duration over the timed steps (its
+    # 24 launches run back to back, each overlapping the previous one's tail)
+    verify_launch_ms = stage["conv_verify"] / (args.steps * cfg.layers)
+    verify_isolated_ms = verify_ms / max(n_verify, 1)
     commit_launch_ms = stage["commit"] / args.steps
     verify_bytes = Bt * VERIFY_BYTES
     commit_bytes = Bt * LAYERS * (COMMIT_BYTES_FIXED + COMMIT_BYTES_PER_NODE * mean_acc)
@@ -417,6 +417,7 @@ def run_ours(args, rank, world, local_rank):
     per_kernel = {
         "score_build_ms": stage["score_build"] / args.steps,
         "conv_verify_ms_per_layer": verify_launch_ms,
+        "conv_verify_isolated_ms_per_layer": verify_isolated_ms,
         "accept_ms": stage["accept"] / args.steps,
         "gdn_commit_ms": commit_launch_ms,
         "score_build_GBps": Bt * SCORE_BYTES / (stage["score_build"] / args.steps / 1e3) / 1e9,
