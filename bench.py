@@ -362,20 +362,39 @@ def run_ours(args, rank, world, local_rank):
         h_tok = torch.empty((Bt, N), dtype=torch.int64, pin_memory=True)
         h_par = torch.empty((Bt, N), dtype=torch.int64, pin_memory=True)
         h_len = torch.empty((Bt,), dtype=torch.int64, pin_memory=True)
-        d_logits, d_x, d_a, d_b = (torch.empty_like(t) for t in (logits, x, a, b))
-        d_root, d_pre1 = torch.empty_like(root), torch.empty_like(pre1)
-        h2d = sum(t.numel() * t.element_size() for t in (h_logits, h_x, h_a, h_b, h_root, h_pre1))
+        hosts = (h_logits, h_x, h_a, h_b, h_root, h_pre1)
+        # two device copies of the step inputs: step i + 1's are copied on a second
+        # stream while step i runs (each buffer is refilled once the step that
+        # read it has finished)
+        bufs = [tuple(torch.empty_like(t) for t in (logits, x, a, b, root, pre1)) for _ in range(2)]
+        cps = torch.cuda.Stream(device=dev)
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        free = [torch.cuda.Event(), torch.cuda.Event()]
+        h2d = sum(t.numel() * t.element_size() for t in hosts)
         d2h = sum(t.numel() * t.element_size() for t in (h_tok, h_par, h_len))
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         s0, s1 = mk(), mk()
+
+        def issue_copy(i):
+            with torch.cuda.stream(cps):
+                if i >= 2:
+                    cps.wait_event(free[i % 2])
+                for d_, h in zip(bufs[i % 2], hosts):
+                    d_.copy_(h, non_blocking=True)
+                copied[i % 2].record(cps)
+
         s0.record(stream)
-        for _ in range(ke):
-            for d_, h in ((d_logits, h_logits), (d_x, h_x), (d_a, h_a), (d_b, h_b), (d_root, h_root),
-                          (d_pre1, h_pre1)):
-                d_.copy_(h, non_blocking=True)
+        cps.wait_stream(stream)
+        issue_copy(0)
+        for i in range(ke):
+            if i + 1 < ke:
+                issue_copy(i + 1)
+            stream.wait_event(copied[i % 2])
+            d_logits, d_x, d_a, d_b, d_root, d_pre1 = bufs[i % 2]
             cyc.step(d_logits, d_root, d_pre1, d_x, d_a, d_b, target_fn)
+            free[i % 2].record(stream)
             h_tok.copy_(cyc.tree["tokens"], non_blocking=True)
             h_par.copy_(cyc.tree["parent"], non_blocking=True)
             h_len.copy_(cyc.accept_len, non_blocking=True)
@@ -387,7 +406,8 @@ def run_ours(args, rank, world, local_rank):
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             ems = float(tt)
         e2e = {"value": world * ke / (ems / 1e3), "unit": "cycles/s", "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(d2h), "steps": ke}
+               "d2h_bytes_per_step": int(d2h), "steps": ke,
+               "pipelined": "step i + 1's inputs copied on a second stream while step i runs"}
     # ---- tree-masked attention verify of one gated full-attention layer (outside the cycle)
     attn = _bench_attention(args, dev, cyc, g, stream) if args.attn else None
     status = int(cyc.status.item())
