@@ -24,7 +24,9 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 
 // ahead: the block `ahead` launches later (about two waves) has its path rows
 // of k and vn prefetched into L2 by this block's warp 0, so that its own
-// dependent row loads (after the path set-up) hit L2 instead of DRAM
+// dependent row loads (after the path set-up) hit L2 instead of DRAM.
+// ahead == 0x7fffffff marks rows that are not 16-byte aligned: no prefetch,
+// scalar row loads.
 __global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args a, int32_t* st, int ahead) {
   extern __shared__ __align__(16) float s_path[];  // [cap][kD] k*w, then [cap][kD] vn
   __shared__ int s_ids[kMaxPath];
@@ -55,7 +57,7 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args
   const float* S0 = a.state_in + (int64_t)l * a.si_sl + slot * a.si_ss + (int64_t)h * a.si_sh;
   float* So = a.state_out + (int64_t)l * a.so_sl + dst * a.so_ss + u * a.so_su + (int64_t)h * a.so_sh;
   const int k4 = (tid & 31) * 4;
-  const int v0 = tid >> 5;  // rows v0, v0 + 8, ..., 16 rows per thread
+  const int v0 = (tid >> 5) * 16;  // rows v0 .. v0 + 15 (the warp's 16 rows, 128 floats each)
   const bool vec = a.si_sk == 1 && a.so_sk == 1 && (a.si_sv % 4 == 0) && (a.so_sv % 4 == 0) &&
                    ((uintptr_t)S0 % 16 == 0) && ((uintptr_t)So % 16 == 0);
   // the state tile does not depend on the path: its loads go out first and
@@ -63,11 +65,11 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args
   float4 acc[16];
   if (vec) {
 #pragma unroll
-    for (int r = 0; r < 16; ++r) acc[r] = __ldcs(reinterpret_cast<const float4*>(S0 + (int64_t)(v0 + 8 * r) * a.si_sv + k4));
+    for (int r = 0; r < 16; ++r) acc[r] = __ldcs(reinterpret_cast<const float4*>(S0 + (int64_t)(v0 + r) * a.si_sv + k4));
   } else {
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
-      const float* p = S0 + (int64_t)(v0 + 8 * r) * a.si_sv + (int64_t)k4 * a.si_sk;
+      const float* p = S0 + (int64_t)(v0 + r) * a.si_sv + (int64_t)k4 * a.si_sk;
       acc[r] = make_float4(p[0], p[a.si_sk], p[2 * a.si_sk], p[3 * a.si_sk]);
     }
   }
@@ -146,11 +148,27 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args
   float (*svv)[kD] = reinterpret_cast<float (*)[kD]>(s_path + (size_t)cap * kD);
   const float* Kb = a.aux_k + (int64_t)l * a.ak_sl + (int64_t)b * a.ak_sb + (int64_t)khead * a.ak_sh;
   const float* Vb = a.aux_vn + (int64_t)l * a.av_sl + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh;
-  for (int i = tid; i < np * kD; i += kThreads) {
-    const int t = i >> 7, d = i & 127;
-    const int id = s_ids[t];
-    skk[t][d] = Kb[(int64_t)id * a.ak_sn + d] * s_w[t];  // (k * w) (fc1_fused.py:39)
-    svv[t][d] = Vb[(int64_t)id * a.av_sn + d];
+  if (ahead != 0x7fffffff) {
+    // 16-byte aligned rows (the launch checked them): one float4 of k and of vn per step
+    for (int i = tid; i < np * (kD / 4); i += kThreads) {
+      const int t = i >> 5, d4 = (i & 31) * 4;
+      const int id = s_ids[t];
+      const float w = s_w[t];
+      float4 kq = *reinterpret_cast<const float4*>(Kb + (int64_t)id * a.ak_sn + d4);
+      kq.x *= w;  // (k * w) (fc1_fused.py:39)
+      kq.y *= w;
+      kq.z *= w;
+      kq.w *= w;
+      *reinterpret_cast<float4*>(&skk[t][d4]) = kq;
+      *reinterpret_cast<float4*>(&svv[t][d4]) = *reinterpret_cast<const float4*>(Vb + (int64_t)id * a.av_sn + d4);
+    }
+  } else {
+    for (int i = tid; i < np * kD; i += kThreads) {
+      const int t = i >> 7, d = i & 127;
+      const int id = s_ids[t];
+      skk[t][d] = Kb[(int64_t)id * a.ak_sn + d] * s_w[t];  // (k * w) (fc1_fused.py:39)
+      svv[t][d] = Vb[(int64_t)id * a.av_sn + d];
+    }
   }
   const float eg = expf(gu);
   __syncthreads();
@@ -163,9 +181,19 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args
   }
   for (int t = 0; t < np; ++t) {
     const float4 kk = *reinterpret_cast<const float4*>(&skk[t][k4]);
+    // the thread's 16 vn entries are contiguous: four 128-bit shared loads
+    float vr[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v4 = *reinterpret_cast<const float4*>(&svv[t][v0 + 4 * q]);
+      vr[4 * q] = v4.x;
+      vr[4 * q + 1] = v4.y;
+      vr[4 * q + 2] = v4.z;
+      vr[4 * q + 3] = v4.w;
+    }
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
-      const float vv = svv[t][v0 + 8 * r];
+      const float vv = vr[r];
       acc[r].x = fmaf(vv, kk.x, acc[r].x);
       acc[r].y = fmaf(vv, kk.y, acc[r].y);
       acc[r].z = fmaf(vv, kk.z, acc[r].z);
@@ -174,11 +202,11 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_commit_kernel(dft_commit_args
   }
   if (vec) {
 #pragma unroll
-    for (int r = 0; r < 16; ++r) __stcs(reinterpret_cast<float4*>(So + (int64_t)(v0 + 8 * r) * a.so_sv + k4), acc[r]);
+    for (int r = 0; r < 16; ++r) __stcs(reinterpret_cast<float4*>(So + (int64_t)(v0 + r) * a.so_sv + k4), acc[r]);
   } else {
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
-      float* p = So + (int64_t)(v0 + 8 * r) * a.so_sv + (int64_t)k4 * a.so_sk;
+      float* p = So + (int64_t)(v0 + r) * a.so_sv + (int64_t)k4 * a.so_sk;
       p[0] = acc[r].x;
       p[a.so_sk] = acc[r].y;
       p[2 * a.so_sk] = acc[r].z;
