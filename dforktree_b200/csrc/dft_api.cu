@@ -9,28 +9,6 @@ int dft_beam_launch(const dft_build_params* p, const float* lp, const int32_t* i
                     int32_t* dev_status, cudaStream_t st);
 int dft_check_build_params(const dft_build_params* p);
 
-namespace {
-
-inline int64_t up256(int64_t x) { return (x + 255) & ~(int64_t)255; }
-
-struct WsLayout {
-  int64_t lp, ids, rest, T, total;
-};
-
-WsLayout ws_layout(const dft_build_params* p) {
-  WsLayout w;
-  const int64_t rows = (int64_t)p->B * p->S;
-  int64_t o = 0;
-  w.lp = o; o = up256(o + rows * p->M * 4);
-  w.ids = o; o = up256(o + rows * p->M * 4);
-  w.rest = o; o = up256(o + rows * 4);
-  w.T = o; o = up256(o + (p->use_ngram ? (int64_t)p->B * (p->S - 1) * p->M * p->M * p->M * 4 : 0));
-  w.total = o;
-  return w;
-}
-
-}  // namespace
-
 extern "C" const char* dft_status_string(int s) {
   switch (s) {
     case DFT_OK: return "ok";
@@ -49,7 +27,7 @@ extern "C" int dft_version(void) { return 10000; }
 
 extern "C" int64_t dft_score_build_workspace_bytes(const dft_build_params* p) {
   if (dft_check_build_params(p)) return -1;
-  return ws_layout(p).total;
+  return dft::build_scratch_layout(p).total;
 }
 
 int dft_pmi_dense_launch(const dft_table* table, const dft_build_params* p, const int32_t* ids, const int64_t* root,
@@ -66,7 +44,7 @@ extern "C" int dft_score_build(const dft_table* table, const dft_build_params* p
   if (!dft::valid_dtype(logits_dtype)) return DFT_ERR_INVALID;
   if (ld_s < p->V || ld_b < (int64_t)p->S * ld_s - (ld_s - p->V)) return DFT_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const WsLayout w = ws_layout(p);
+  const dft::BuildScratch w = dft::build_scratch_layout(p);
   char* ws = reinterpret_cast<char*>(workspace);
   float* lp = reinterpret_cast<float*>(ws + w.lp);
   int32_t* ids = reinterpret_cast<int32_t*>(ws + w.ids);

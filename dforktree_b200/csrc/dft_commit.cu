@@ -224,6 +224,9 @@ extern "C" int dft_gdn_commit(const dft_commit_args* a, int32_t* dev_status, voi
   if (a->L <= 0 || a->B <= 0 || a->N <= 0 || a->Hk <= 0 || a->Hv <= 0 || a->P < 0 || a->E <= 0)
     return DFT_ERR_INVALID;
   if (a->Hv % a->Hk) return DFT_ERR_INVALID;
+  // with a zero end stride every end node of a request writes the same output
+  // tile (the in-place form): more than one end would race on it
+  if (a->so_su == 0 && a->E > 1) return DFT_ERR_INVALID;
   if (a->Dk != kD || a->Dv != kD || a->P > kMaxPath || a->N > kMaxNodes) return DFT_ERR_UNSUPPORTED;
   const int64_t blocks = (int64_t)a->E * a->L * a->B * a->Hv;
   if (blocks > 0x7fffffffll) return DFT_ERR_UNSUPPORTED;

@@ -48,6 +48,27 @@ __device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v
 
 inline bool valid_dtype(int d) { return d == DFT_F32 || d == DFT_BF16 || d == DFT_F16; }
 
+// Score + build scratch layout (drafter lp / ids / rest rows, then the dense
+// order-3 PMI tensor T), shared by dft_score_build's caller workspace and
+// dft_score_build_static's fixed array, so both use the same offsets.
+struct BuildScratch {
+  int64_t lp, ids, rest, T, total;
+};
+
+inline int64_t up256(int64_t x) { return (x + 255) & ~(int64_t)255; }
+
+inline BuildScratch build_scratch_layout(const dft_build_params* p) {
+  BuildScratch w;
+  const int64_t rows = (int64_t)p->B * p->S;
+  int64_t o = 0;
+  w.lp = o; o = up256(o + rows * p->M * 4);
+  w.ids = o; o = up256(o + rows * p->M * 4);
+  w.rest = o; o = up256(o + rows * 4);
+  w.T = o; o = up256(o + (p->use_ngram ? (int64_t)p->B * (p->S - 1) * p->M * p->M * p->M * 4 : 0));
+  w.total = o;
+  return w;
+}
+
 // ---------------------------------------------------------------- SiLU --
 // silu(x) = x / (1 + e^-x) with e^-x = 2^(-x log2 e) from the hardware
 // base-2 exponential and 1 / d from the hardware reciprocal (both the

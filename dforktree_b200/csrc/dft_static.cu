@@ -10,6 +10,8 @@
 // held by every GPU that loads the library until the process exits.
 #include "dft_common.cuh"
 
+#include <cuda.h>
+
 #include <mutex>
 
 int dft_score_launch(const dft_build_params* p, const void* logits, int32_t dtype, int64_t ld_b, int64_t ld_s,
@@ -30,23 +32,46 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_score_build_scratch[kStaticScratchBytes];
 
+// cuCtxGetCurrent through the runtime's driver entry point (no -lcuda at link time)
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(p);
+    return static_cast<CtxGetCurrentFn>(nullptr);
+  }();
+  return fn;
+}
+
 std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
-inline int64_t up256(int64_t x) { return (x + 255) & ~(int64_t)255; }
-
-// Device address of the scratch array for the current device, resolved once
-// per device with that device current (host code cannot use the symbol's
-// name as a device pointer).
+// Device address of the scratch array for the current device, resolved with
+// that device current the first time the device is used (host code cannot use
+// the symbol's name as a device pointer).  The address belongs to the device's
+// current context: if that context changed since (cudaDeviceReset, a reset of
+// the primary context), it is resolved again in the new one.
 int scratch_for_current_device(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return DFT_ERR_NO_DEVICE;
   if (dev >= kMaxDevices) return DFT_ERR_UNSUPPORTED;
+  // make the runtime's context for the device current on this thread before
+  // asking the driver which context that is
+  if (cudaSetDevice(dev) != cudaSuccess) return DFT_ERR_CUDA;
+  CtxGetCurrentFn get_ctx = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (!get_ctx || get_ctx(&ctx) != CUDA_SUCCESS || !ctx) return DFT_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_ptr[dev]) {
+  if (!g_scratch_ptr[dev] || g_scratch_ctx[dev] != ctx) {
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_score_build_scratch) != cudaSuccess || !ptr) return DFT_ERR_CUDA;
     g_scratch_ptr[dev] = ptr;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_ptr[dev];
   return DFT_OK;
@@ -65,23 +90,17 @@ extern "C" int dft_score_build_static(const dft_table* table, const dft_build_pa
   if (p->use_ngram && !table) return DFT_ERR_INVALID;
   if (!dft::valid_dtype(logits_dtype)) return DFT_ERR_INVALID;
   if (ld_s < p->V || ld_b < (int64_t)p->S * ld_s - (ld_s - p->V)) return DFT_ERR_INVALID;
-  // scratch layout identical to dft_score_build's workspace
-  const int64_t rows = (int64_t)p->B * p->S;
-  const int64_t o_lp = 0;
-  const int64_t o_ids = up256(o_lp + rows * p->M * 4);
-  const int64_t o_rest = up256(o_ids + rows * p->M * 4);
-  const int64_t o_T = up256(o_rest + rows * 4);
-  const int64_t total =
-      up256(o_T + (p->use_ngram ? (int64_t)p->B * (p->S - 1) * p->M * p->M * p->M * 4 : 0));
-  if (total > kStaticScratchBytes) return DFT_ERR_CAPACITY;
+  // the same scratch layout as dft_score_build's workspace
+  const dft::BuildScratch w = dft::build_scratch_layout(p);
+  if (w.total > kStaticScratchBytes) return DFT_ERR_CAPACITY;
   void* base = nullptr;
   rc = scratch_for_current_device(&base);
   if (rc) return rc;
   char* ws = reinterpret_cast<char*>(base);
-  float* lp = reinterpret_cast<float*>(ws + o_lp);
-  int32_t* ids = reinterpret_cast<int32_t*>(ws + o_ids);
-  float* rest = reinterpret_cast<float*>(ws + o_rest);
-  float* T = p->use_ngram ? reinterpret_cast<float*>(ws + o_T) : nullptr;
+  float* lp = reinterpret_cast<float*>(ws + w.lp);
+  int32_t* ids = reinterpret_cast<int32_t*>(ws + w.ids);
+  float* rest = reinterpret_cast<float*>(ws + w.rest);
+  float* T = p->use_ngram ? reinterpret_cast<float*>(ws + w.T) : nullptr;
   // every scratch byte read below is written earlier in the same call (score
   // writes all lp / ids / rest rows, the PMI kernel all of T): nothing needs
   // clearing between calls

@@ -169,7 +169,10 @@ DFT_API int dft_score_build(const dft_table* table, const dft_build_params* p, c
  * held by every GPU that loads the library until the process exits; larger
  * shapes return DFT_ERR_CAPACITY.  The first call on a device resolves the
  * array's device address (cudaGetSymbolAddress, with that device current);
- * make that first call before any stream capture.  All calls share the one
+ * make that first call before any stream capture.  A device reset
+ * (cudaDeviceReset) discards the array's contents and its address; the next
+ * call sees the new context and resolves the address again, so after a reset
+ * make one call outside any capture first.  All calls share the one
  * array: calls whose kernels overlap on the GPU (other streams, other host
  * threads) race.  Each call writes every scratch byte it reads, so nothing
  * carries over between calls.  Allocates nothing. */
@@ -291,7 +294,8 @@ DFT_API int dft_gdn_tree_verify(const dft_gdn_args* a, int32_t* dev_status, void
  *   S_u = e^{G_u} S0 + sum_{t in path[b], t anc-or-self of u} e^{G_u-G_t} vn_t k_t^T
  * S0 (l, slot, h, v, k) = state_in[l*si_sl + slot*si_ss + h*si_sh + v*si_sv + k*si_sk];
  * S_u written to state_out[l*so_sl + dst*so_ss + u*so_su + h*so_sh + v*so_sv + k*so_sk]
- * (so_su = 0 and dst = slot: in place into the pool, E must be 1).        */
+ * (so_su = 0 and dst = slot: in place into the pool; so_su = 0 with E > 1
+ * returns DFT_ERR_INVALID, since every end would write the same tile).     */
 typedef struct {
   int32_t L, B, N, Hk, Hv, Dk, Dv, P, E;
   const float* state_in; int64_t si_sl, si_ss, si_sh, si_sv, si_sk;

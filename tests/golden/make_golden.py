@@ -263,11 +263,14 @@ def gen_commit(mods, out_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("DFORKTREE_REF", "/root/reference/dforktree"))
+    ap.add_argument("--ref", default=os.environ.get("DFORKTREE_REF"),
+                    help="the reference's dforktree/ source directory (or set DFORKTREE_REF)")
     ap.add_argument("--out", default=HERE)
     ap.add_argument("--only", default="")
     ap.add_argument("--no-config0", action="store_true")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference's dforktree/ directory with --ref or DFORKTREE_REF")
     mods = _load_reference(args.ref)
     captured = _patch_path_fn(mods)
     only = set(args.only.split(",")) if args.only else {"ngram", "builder", "gdn", "conv", "commit"}

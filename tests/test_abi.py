@@ -53,6 +53,12 @@ def test_invalid_arguments_are_rejected_on_the_host(lib):
     assert lib.dft_score_build_workspace_bytes(ctypes.byref(p)) >= 23 * 4096 * 4
     assert lib.dft_gdn_tree_verify(None, None, None) == 1
     assert lib.dft_gdn_commit(None, None, None) == 1
+    # in-place commit (zero end stride) with two end nodes would race on one tile:
+    # rejected from the arguments alone (the pointers are never dereferenced)
+    fake = 1 << 20
+    ca = L.CommitArgs(L=1, B=1, N=32, Hk=16, Hv=32, Dk=128, Dv=128, P=24, E=2, state_in=fake, state_out=fake,
+                      so_su=0, aux_k=fake, aux_vn=fake, aux_g=fake, anc=fake, path=fake, ends=fake)
+    assert lib.dft_gdn_commit(ctypes.byref(ca), None, None) == 1
     assert lib.dft_tree_conv(None, None, None) == 1
     assert lib.dft_conv_commit(None, None, None) == 1
     assert lib.dft_tree_attn(None, None, None, None) == 1
