@@ -7,11 +7,19 @@ One step = one full cycle over the batch (see dforktree_b200/cycle.py):
 score+build of 64 requests (S=24 positions over V=248,320 fp32 logits, the
 config-0 n-gram table shared), tree conv + GDN tree verify on each of the 24
 GDN layers of the Qwen3.5-9B shape (Hk=16, Hv=32, D=128), greedy tree
-acceptance against synthetic target tokens (accepted lengths uniform 1..24),
-and the closed-form commit of every layer's state.  Data is synthetic (seeded;
+acceptance against a target stand-in that agrees with the draft along the
+deepest node's path for a drawn length U[1,24] (cut at the path's end), and
+the closed-form commit of every layer's state.  Data is synthetic (seeded;
 random-init layer weights).  Under torchrun every rank runs its own batch of
 64 requests (weak scaling, no collective on the data path); timing is CUDA
 events on each rank, the maximum over ranks.
+
+The line also carries `config4`: BASELINE config 4 -- 256 requests split over
+the ranks (strong scaling), the hybrid 32-layer stack with the 8 gated
+attention layers inside the cycle, chain-first trees with accepted lengths
+U[1,24].  `--impl reference` times whole cycles of the reference on the host
+cores and, in a child process, the reference's own Triton / torch GPU path
+(`reference_gpu`).
 """
 from __future__ import annotations
 
@@ -29,9 +37,10 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "draft-tree cycles/sec (score+build+GDN verify+commit) at batch 64; % roofline"
-WORKLOAD = ("dforktree cycle: batch 64/GPU, S=24, V=248320 fp32 logits, 2M+8M n-gram table, B=32 nodes, M=16, "
-            "24 Qwen3.5-9B GDN layers (tree conv + verify, Hk=16 Hv=32 D=128, bf16 activations, fp32 state), "
-            "greedy accept (len U[1,24]), in-place commit")
+WORKLOAD = ("dforktree cycle (BASELINE config 1 + GDN verify/commit): batch 64/GPU, S=24, V=248320 fp32 logits, "
+            "2M+8M n-gram table, B=32 nodes, M=16, 24 Qwen3.5-9B GDN layers (tree conv + verify, Hk=16 Hv=32 "
+            "D=128, bf16 activations, fp32 state), greedy accept along the deepest node's path (drawn length "
+            "U[1,24], cut at the path's end), in-place commit")
 S, V, N, M, LAYERS, HK, HV, D = 24, 248320, 32, 16, 24, 16, 32, 128
 C_CONV = 2 * HK * D + HV * D
 # algorithmic bytes per unit (per layer-request): state in, q / k / v in, gates, o out
@@ -59,86 +68,137 @@ def _peaks():
 
 
 # --------------------------------------------------------- CPU baseline ----
-def _cpu_job_build(args):
-    """Oracle score+build for one request (worker process)."""
-    import numpy as np
-    from oracle import builder as OB
-    from oracle import ngram as ON
-    tdir, seed = args
-    table = {k[:-4]: np.load(os.path.join(tdir, k), mmap_mode="r") for k in os.listdir(tdir) if k.endswith(".npy")}
-    ng = ON.NGramOracle(table, beta3=60.0)
-    from dforktree_b200 import synth
-    logits = synth.make_logits(S, V, seed=seed)
-    t = time.perf_counter()
-    OB.builder_run(logits, 5, 7, ng, N=N)
-    return time.perf_counter() - t
+def _ref_dir():
+    """The reference's dforktree/ sources as installed under baseline/_ref
+    (pip install --target; travels with the tree), or None."""
+    d = os.path.join(ROOT, "baseline", "_ref", "dforktree")
+    return d if os.path.isfile(os.path.join(d, "fc1_builder.py")) else None
 
 
-def _cpu_job_layer(seed):
-    """Oracle tree conv + GDN verify + commit for one layer-request."""
+_W = {}    # per-worker state of the CPU pool
+
+
+def _cpu_init(tdir, npz, ref_dir, n_logits, n_layers):
+    """Worker set-up (spawned, single-threaded): the n-gram table, a few
+    request inputs, and the builder -- the reference's own torch code when its
+    sources are installed, else the numpy port."""
+    for k in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[k] = "1"
+    import multiprocessing as mp
+
     import numpy as np
     from dforktree_b200 import synth
-    from oracle import builder as OB
-    from oracle import gdn as OG
+    wid = (mp.current_process()._identity or (0,))[0]
+    _W["logits"] = [synth.make_logits(S, V, seed=7000 + 97 * wid + i) for i in range(n_logits)]
+    _W["layers"] = [_layer_inputs(9000 + 97 * wid + i) for i in range(n_layers)]
+    if ref_dir:
+        import torch
+        torch.set_num_threads(1)
+        from oracle import reference_shim as RS
+        mods = RS.load_reference(ref_dir, kernels=False)
+        RS.patch_path_fn(mods)
+        ng = mods["ngram_gpu"].NGramGPU(npz, "cpu", beta3=60.0)       # fc1_builder.py:17
+        _W["builder"] = RS.cpu_builder(mods, ng, S, N)
+        _W["torch"] = torch
+    else:
+        from oracle import ngram as ON
+        table = {k[:-4]: np.load(os.path.join(tdir, k), mmap_mode="r") for k in os.listdir(tdir) if k.endswith(".npy")}
+        _W["ng"] = ON.NGramOracle(table, beta3=60.0)
+
+
+def _layer_inputs(seed):
+    import numpy as np
+    from dforktree_b200 import synth
     d = synth.make_gdn_inputs(N, HK, HV, D, seed=seed)
     rng = np.random.default_rng(seed)
-    x = rng.standard_normal((N, C_CONV)).astype(np.float32)
-    cs = rng.standard_normal((C_CONV, 3)).astype(np.float32)
-    w = rng.standard_normal((C_CONV, 4)).astype(np.float32)
-    t = time.perf_counter()
+    d["x"] = rng.standard_normal((N, C_CONV)).astype(np.float32)
+    d["cs"] = rng.standard_normal((C_CONV, 3)).astype(np.float32)
+    d["w"] = rng.standard_normal((C_CONV, 4)).astype(np.float32)
+    return d
+
+
+def _cpu_job(job):
+    """One unit of a cycle on the host: a request's score+build ("b") or a
+    layer-request's tree conv + GDN verify + closed-form commit ("l")."""
+    kind, i = job
+    if kind == "b":
+        lg = _W["logits"][i % len(_W["logits"])]
+        if "builder" in _W:
+            torch = _W["torch"]
+            b = _W["builder"]
+            b.logits = torch.from_numpy(lg)
+            b.root.fill_(5)
+            b.pre1.fill_(7)
+            b.run()                                                     # fc1_builder.py:26-47
+        else:
+            from oracle import builder as OB
+            OB.builder_run(lg, 5, 7, _W["ng"], N=N)
+        return kind
+    from oracle import builder as OB
+    from oracle import gdn as OG
+    d = _W["layers"][i % len(_W["layers"])]
     _, _, cidx = OB.tree_struct(d["parent"], 4)
-    OG.tree_conv(x, cs, w, None, cidx)
-    o, k, vn, G = OG.tree_gdn(d["y"], d["a"], d["b"], d["A_log"], d["dt_bias"], d["pool"], 0, d["anc"], HK, HV, D, D)
+    OG.tree_conv(d["x"], d["cs"], d["w"], None, cidx)
+    _, k, vn, G = OG.tree_gdn(d["y"], d["a"], d["b"], d["A_log"], d["dt_bias"], d["pool"], 0, d["anc"], HK, HV, D, D)
     u = int(d["path"][-1])
     for h in range(HV):
         OG.snapshot(d["pool"][0, h], k[h], vn[h], G[h], d["anc"], d["path"], u)
-    return time.perf_counter() - t
+    return kind
 
 
-class CpuSampler:
-    """The oracle port timed on the host cores for the bench workload: a spawn
-    pool of `workers` single-threaded processes sharing the n-gram table
-    (memory-mapped), warmed once; `rate()` runs a bounded sample and scales it
-    to one batch-64 cycle."""
+class CpuCycle:
+    """The cycle on the host cores, whole cycles at a time: a spawn pool of
+    `workers` single-threaded processes runs every unit of one batch-64 cycle
+    (64 score+builds and 64 x 24 layer-request conv+verify+commits) per
+    `cycle()`, timed by wall clock from the first job to the last result.
+    Score+build is the reference's own torch code (fc1_builder / tree_ops /
+    ngram_gpu from its installed sources, the missing path closure supplied);
+    the GDN conv / verify / commit, which the reference has only as Triton
+    kernels, run as the numpy port of those kernels."""
 
-    def __init__(self, workers: int):
+    def __init__(self, workers: int, batch: int = 64, layers: int = LAYERS):
         import multiprocessing as mp
 
         import numpy as np
 
         from dforktree_b200 import synth
-        self.workers = workers
+        self.workers, self.batch, self.layers = workers, batch, layers
+        self.ref_dir = _ref_dir()
         table = synth.make_ngram_table(V, 2_000_000, 8_000_000, seed=0)
         self.tdir = tempfile.mkdtemp(prefix="dft_table_")
-        for k, v in table.items():
-            np.save(os.path.join(self.tdir, k + ".npy"), np.asarray(v))
-        self._env = {k: os.environ.get(k) for k in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")}
-        for k in self._env:
-            os.environ[k] = "1"
-        self.pool = mp.get_context("spawn").Pool(workers)
-        self.pool.map(_cpu_job_layer, [10_000 + i for i in range(workers)])
-        self.pool.map(_cpu_job_build, [(self.tdir, 10_000 + i) for i in range(workers)])
+        self.npz = os.path.join(self.tdir, "table.npz")
+        if self.ref_dir:
+            np.savez(self.npz, **table)
+        else:
+            for k, v in table.items():
+                np.save(os.path.join(self.tdir, k + ".npy"), np.asarray(v))
+        del table
+        self.pool = mp.get_context("spawn").Pool(workers, initializer=_cpu_init,
+                                                 initargs=(self.tdir, self.npz, self.ref_dir, 2, 2))
+        # one pass of every job kind on every worker before any timing
+        self.pool.map(_cpu_job, [("b", i) for i in range(workers)] + [("l", i) for i in range(workers)], chunksize=1)
 
-    def rate(self, builds_per_worker: int = 1, layers_per_worker: int = 2, seed: int = 0):
-        w = self.workers
-        tb = self.pool.map(_cpu_job_build, [(self.tdir, seed * 1000 + i) for i in range(w * builds_per_worker)])
-        tl = self.pool.map(_cpu_job_layer, [seed * 1000 + i for i in range(w * layers_per_worker)])
-        # concurrent workers: throughput = units / (total compute time / workers)
-        rate_b = len(tb) / (sum(tb) / w)
-        rate_l = len(tl) / (sum(tl) / w)
-        cycle_s = 64 / rate_b + 64 * LAYERS / rate_l
-        sample = (f"{len(tb)} request score+builds and {len(tl)} layer-request conv+verify+commits "
-                  f"(of 64 and {64 * LAYERS} per cycle) on {w} single-threaded processes, scaled to one cycle")
-        return 1.0 / cycle_s, sample, dict(build_s=sum(tb) / len(tb), layer_s=sum(tl) / len(tl))
+    @property
+    def kind(self):
+        # the GDN stages (most of the time) always run as the port
+        return "port"
+
+    def describe(self):
+        who = ("the reference's own torch builder (fc1_builder / tree_ops / ngram_gpu, installed sources, "
+               "missing path closure supplied)" if self.ref_dir else "the numpy port of the builder")
+        return (f"whole cycles: {self.batch} score+builds by {who} and {self.batch} x {self.layers} layer-request "
+                f"conv+verify+commits by the numpy port of the reference's Triton kernels, per step, on "
+                f"{self.workers} single-threaded processes (wall clock)")
+
+    def cycle(self) -> float:
+        jobs = [("b", i) for i in range(self.batch)] + [("l", i) for i in range(self.batch * self.layers)]
+        t = time.perf_counter()
+        self.pool.map(_cpu_job, jobs, chunksize=8)
+        return time.perf_counter() - t
 
     def close(self):
         self.pool.close()
         self.pool.join()
-        for k, v in self._env.items():
-            if v is None:
-                os.environ.pop(k, None)
-            else:
-                os.environ[k] = v
         for f in os.listdir(self.tdir):
             os.unlink(os.path.join(self.tdir, f))
         os.rmdir(self.tdir)
@@ -236,6 +296,7 @@ def run_ours(args, rank, world, local_rank):
     from dforktree_b200 import build as B
     from dforktree_b200 import kernels as K
     from dforktree_b200 import synth
+    from dforktree_b200 import workload as WL
     from dforktree_b200.cycle import CycleConfig, DraftTreeCycle
 
     if rank == 0:
@@ -248,27 +309,21 @@ def run_ours(args, rank, world, local_rank):
     table_np = synth.make_ngram_table(V, 2_000_000, 8_000_000, seed=0)
     from dforktree_b200.ngram_gpu import load_npz_arrays
     table = K.Table(load_npz_arrays(table_np), beta3=60.0, device=dev)
+    del table_np
+    # config 4 first: its buffers (~63 GB at 256 requests on one GPU) are freed before the headline's
+    c4 = _bench_config4(args, rank, world, dev, table) if args.requests > 0 and not args.profile else None
     cyc = DraftTreeCycle(cfg, table, dev, seed=rank)
     g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
+    g.manual_seed(4321 + rank)
     Bt = cfg.B
     # synthetic per-step inputs, resident in HBM (larger than L2: no flush needed)
-    logits = torch.randn(Bt, S, V, device=dev, generator=g) * 3.0
-    pk = torch.randint(0, V, (Bt, S), device=dev, generator=g)
-    logits.view(-1, V)[torch.arange(Bt * S, device=dev), pk.view(-1)] += 6.0
-    root = torch.randint(0, V, (Bt,), device=dev, generator=g)
-    pre1 = torch.randint(0, V, (Bt,), device=dev, generator=g)
-    x = torch.randn(cfg.layers, Bt, N, cfg.C, device=dev, generator=g).to(torch.bfloat16)
-    a = torch.randn(cfg.layers, Bt, N, HV, device=dev, generator=g).to(torch.bfloat16)
-    b = torch.randn(cfg.layers, Bt, N, HV, device=dev, generator=g).to(torch.bfloat16)
-    acc_len = torch.randint(1, 25, (Bt,), device=dev, generator=g)
+    inp = WL.cycle_inputs(cfg, dev, seed=1234 + rank)
+    logits, root, pre1, x, a, b = (inp[k] for k in ("logits", "root", "pre1", "x", "a", "b"))
+    acc_len = inp["acc_len"]
 
     def target_fn(tree):
-        # target model stand-in: agrees with the first-child chain up to the drawn length
-        nx = tree["nxt"]
-        tgt = torch.gather(tree["tokens"], 1, nx.clamp(min=0))
-        keep = (nx >= 0) & (tree["depth"] + 1 < acc_len[:, None])
-        return torch.where(keep, tgt, torch.full_like(tgt, -1))
+        # target-model stand-in: agrees with the draft along the deepest node's path up to the drawn length
+        return WL.path_target(tree, acc_len)
 
     stream = torch.cuda.current_stream(dev)
 
@@ -454,16 +509,94 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": round(value, 3), "unit": "cycles/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch_per_gpu": Bt, "S": S, "V": V, "N": N, "M": M, "layers": cfg.layers,
-                   "Hk": HK, "Hv": HV, "D": D, "parallelism": f"request-sharded x{world}",
-                   "l2": "inputs larger than L2 (logits 1.5 GB, states 3 GiB per GPU); no flush"},
+        "config": _config(Bt, cfg.layers, world),
         "roofline": roof, "stages": {k: round(v, 4) for k, v in per_kernel.items()},
         "gpu_launches": cyc.launches_per_step * args.steps, "dev_status": status,
     }
     if e2e is not None:
         line["e2e"] = e2e
     line["clocks"] = clk.summary()
+    if c4 is not None:
+        line["config4"] = c4
     return line
+
+
+CONFIG4 = ("BASELINE config 4 at every N: 256 requests split over the GPUs (strong scaling), each a cycle of "
+           "score+build (chain-first trees, so the drawn accepted lengths U[1,24] are reachable) -> 32 Qwen3.5-9B "
+           "layers in model order (24 GDN: tree conv + verify; 8 gated attention: tree-masked attention over a "
+           "4K-token prefix + the tree, 16 q / 4 kv heads at dim 256) -> greedy accept -> in-place commit")
+
+
+def _bench_config4(args, rank, world, dev, table):
+    """The hybrid-stack cycle of config 4: this rank's share of args.requests,
+    W warm-up + K timed cycles (CUDA events, barrier + sync on both sides, max
+    over ranks); value = whole-job cycles/s (every cycle covers all requests)."""
+    import torch
+    import torch.distributed as dist
+
+    from dforktree_b200 import sharding
+    from dforktree_b200 import workload as WL
+    from dforktree_b200.cycle import CycleConfig, DraftTreeCycle
+
+    shard = sharding.partition(args.requests, world)[rank]
+    if shard.count == 0:
+        raise SystemExit("config 4: more ranks than requests")
+    cfg = CycleConfig(B=shard.count, layers=LAYERS, attn_layers=8, chain_first=True)
+    cyc = DraftTreeCycle(cfg, table, dev, seed=100 + rank)
+    inp = WL.cycle_inputs(cfg, dev, seed=5678 + rank)
+    logits, root, pre1, x, a, b, q = (inp[k] for k in ("logits", "root", "pre1", "x", "a", "b", "q"))
+    acc_len = inp["acc_len"]
+    stream = torch.cuda.current_stream(dev)
+    mk = lambda: torch.cuda.Event(enable_timing=True)
+
+    def one(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        cyc.build(logits, root, pre1)
+        if ev is not None:
+            ev[1].record(stream)
+        cyc.verify(x, a, b, q)
+        if ev is not None:
+            ev[2].record(stream)
+        cyc.accept(WL.path_target(cyc.tree, acc_len))
+        cyc.commit(x)
+        if ev is not None:
+            ev[3].record(stream)
+
+    for _ in range(max(args.warmup, 1)):
+        one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [[mk() for _ in range(4)] for _ in range(args.steps)]
+    t0, t1 = mk(), mk()
+    t0.record(stream)
+    for ev in evs:
+        one(ev)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    ms_max = ms
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_max = float(tt)
+    k = args.steps
+    stages = {"score_build_ms": sum(e[0].elapsed_time(e[1]) for e in evs) / k,
+              "verify_32_layers_ms": sum(e[1].elapsed_time(e[2]) for e in evs) / k,
+              "accept_commit_ms": sum(e[2].elapsed_time(e[3]) for e in evs) / k,
+              "mean_accept_len": float(cyc.accept_len.float().mean())}
+    status = int(cyc.status.item())
+    out = {"workload": CONFIG4, "requests": args.requests, "requests_per_gpu": shard.count,
+           "value": round(k / (ms_max / 1e3), 3), "unit": "cycles/s", "ms_per_step": round(ms_max / k, 4),
+           "scaling": "strong", "stages": {kk: round(v, 4) for kk, v in stages.items()},
+           "gpu_launches": cyc.launches_per_step * k, "dev_status": status}
+    del cyc, inp, logits, x, a, b, q
+    torch.cuda.empty_cache()
+    return out
 
 
 def _attention_inputs(dev, Bt, anc, g):
@@ -535,24 +668,164 @@ def _traffic():
 
 
 # ----------------------------------------------------------- reference -----
+def _config(Bt, layers, world):
+    return {"workload": WORKLOAD, "batch_per_gpu": Bt, "S": S, "V": V, "N": N, "M": M, "layers": layers,
+            "Hk": HK, "Hv": HV, "D": D, "parallelism": f"request-sharded x{world}",
+            "l2": "inputs larger than L2 (logits 1.5 GB, states 3 GiB per GPU); no flush"}
+
+
 def run_reference(args):
-    rates = []
+    """The reference arm: whole cycles on the host cores (CpuCycle), W warm-up
+    + K timed steps, plus the reference's own Triton / torch GPU path on GPU 0
+    (a child process, so that a failure there leaves this line intact)."""
     workers = max(1, min(os.cpu_count() or 1, 64))
-    sampler = CpuSampler(workers)
+    cpu = CpuCycle(workers, args.batch, args.layers)
+    times = []
     try:
         for step in range(args.warmup + args.steps):
-            r, sample, _ = sampler.rate(1, 2, seed=step)
+            t = cpu.cycle()
             if step >= args.warmup:
-                rates.append(r)
+                times.append(t)
+        sample, kind = cpu.describe(), cpu.kind
     finally:
-        sampler.close()
-    v = statistics.median(rates)
-    return {"impl": "reference", "metric": METRIC, "value": v, "unit": "cycles/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch_per_gpu": 64},
-            "cpu_baseline": {"value": v, "unit": "cycles/s", "cores": workers, "kind": "port", "sample": sample},
+        cpu.close()
+    total = sum(times)
+    v = len(times) / total
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "cycles/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": _config(args.batch, args.layers, args.gpus),
+            "cpu_baseline": {"value": v, "unit": "cycles/s", "cores": workers, "kind": kind, "sample": sample},
             "e2e": {"value": v, "unit": "cycles/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_reference_gpu:
+        line["reference_gpu"] = _reference_gpu_child(args)
+    return line
+
+
+def _reference_gpu_child(args):
+    cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference-gpu", "--steps", str(args.steps),
+           "--warmup", str(args.warmup), "--batch", str(args.batch), "--layers", str(args.layers)]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE")}
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=1500, env=env)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "reference GPU path did not finish within 1500 s"}
+    for ln in reversed(r.stdout.strip().splitlines()):
+        if ln.startswith("{"):
+            return json.loads(ln)
+    tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+    return {"unavailable": f"reference GPU path exited {r.returncode}: {tail[0][:300]}"}
+
+
+def run_reference_gpu(args):
+    """The reference's own GPU path for the same cycle on GPU 0, request by
+    request as the plugin runs it (it asserts one request per verify,
+    fc1_branch64.py:13): fc1_builder.Builder (torch, CUDA-graph replay), per GDN
+    layer the conv hook's Triton kernel (fc1_conv.py:8-27, 35-44) and
+    tree_kernels.tree_gdn_split (tree_kernels.py:193-208) with the hook's
+    arguments (fc1_fused.py:59-75), greedy acceptance along the same target
+    path (torch ops on the device), then fc1_fused.snapshots (fc1_fused.py:27-49,
+    82) and the copy of the accepted snapshot / conv window into the request's
+    slot that SGLang's commit then makes.  Same seeded inputs as our rank 0.
+    Device time over K cycles (CUDA events), W warm-up cycles first."""
+    ref = _ref_dir()
+    if ref is None:
+        return {"unavailable": "reference sources not installed under baseline/_ref"}
+    import numpy as np
+    import torch
+
+    from dforktree_b200 import synth
+    from dforktree_b200 import workload as WL
+    from dforktree_b200.cycle import CycleConfig
+    from oracle import reference_shim as RS
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    tdir = tempfile.mkdtemp(prefix="dft_ref_")
+    npz = os.path.join(tdir, "table.npz")
+    np.savez(npz, **synth.make_ngram_table(V, 2_000_000, 8_000_000, seed=0))
+    os.environ["FC1_TREE_N"] = str(N)
+    os.environ["FC1_NGRAM_PATH"] = npz
+    os.environ.pop("FC1_CHAIN_FIRST", None)
+    mods = RS.load_reference(ref, kernels=True)
+    RS.patch_path_fn(mods)
+    import triton
+    TK, FF, FC = mods["tree_kernels"], mods["fc1_fused"], mods["fc1_conv"]
+    cfg = CycleConfig(B=args.batch, layers=args.layers)
+    Ls, Bt, C = cfg.layers, cfg.B, cfg.C
+    inp = WL.cycle_inputs(cfg, dev, seed=1234)
+    logits, root, pre1, x, a, b = (inp[k] for k in ("logits", "root", "pre1", "x", "a", "b"))
+    acc_len = inp["acc_len"]
+    builder = mods["fc1_builder"].Builder(logits[0])           # captures its CUDA graph (fc1_builder.py:20-23)
+    os.unlink(npz)
+    os.rmdir(tdir)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    conv_w = (torch.randn(Ls, C, 4, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    A_log = (torch.randn(Ls, HV, device=dev, generator=g) * 0.5).float()
+    neg = -A_log.exp()
+    dt_bias = (torch.randn(Ls, HV, device=dev, generator=g) * 0.5).float()
+    conv_state = torch.randn(Ls, Bt, C, 3, device=dev, generator=g).to(torch.bfloat16)
+    pool = torch.randn(Ls, Bt, HV, D, D, device=dev, generator=g) * 0.02      # [L, slots, H, V, K] like SGLang's
+    keys = torch.empty(Ls, HV, N, D, device=dev)                               # Context (fc1_fused.py:12-20)
+    values = torch.empty_like(keys)
+    gains = torch.empty(Ls, HV, N, device=dev)
+    anc_buf = torch.eye(N, device=dev)
+    cidx_buf = torch.empty(N, 4, dtype=torch.int32, device=dev)
+    iw = torch.empty(Ls, 1, N, C, 3, dtype=torch.bfloat16, device=dev)        # intermediate conv window, one slot
+    inter = torch.empty(Ls, 1, N, HV, D, D, device=dev)                         # intermediate_ssm, one slot
+    slots32 = torch.arange(Bt, dtype=torch.int32, device=dev)
+    slots64 = slots32.long()
+    zero = torch.zeros(1, dtype=torch.int64, device=dev)
+    pos = torch.arange(LAYERS, device=dev)
+
+    def request(r):
+        tokens, depth, parent, anc, nxt, sib = builder(logits[r], root[r:r + 1], pre1[r:r + 1])
+        anc_buf.copy_(anc)                                                # fc1_branch64.py:28-30
+        cidx_buf.copy_(builder.cidx)
+        for l in range(Ls):
+            xv = x[l, r].t().unsqueeze(0)                                # [1, C, N] channels-first
+            y = torch.empty(1, N, C, dtype=x.dtype, device=dev)
+            cs = conv_state[l]
+            FC.conv[(N, triton.cdiv(C, 256))](cs, xv, conv_w[l], xv, cidx_buf, slots64[r:r + 1], zero, iw[l], y, C,
+                                              *cs.stride(), xv.stride(1), xv.stride(2), *iw[l].stride(),
+                                              BIAS=False, BC=256, num_warps=4)
+            TK.tree_gdn_split(y[0], a[l, r], b[l, r], A_log[l], dt_bias[l], pool[l][0].transpose(-1, -2), anc_buf,
+                              HK, HV, D, D, aux=(keys[l], values[l], gains[l]), neg_exp_A=neg[l],
+                              state_indices=slots32[r:r + 1], state_slot_stride=pool[l].stride(0))
+        # greedy acceptance along the target path (the deepest node's), on the device
+        d = builder.depth
+        on_path = anc_buf[d.argmax()] > 0.5
+        order = torch.where(on_path, d, N + 1).argsort()
+        n_acc = torch.minimum(acc_len[r], on_path.sum())
+        accept_index = torch.where(pos < n_acc, order[:LAYERS], -1)[None]
+        last = order.gather(0, (n_acc - 1).view(1))
+        ends = torch.cat((last, torch.full_like(last, -1)))
+        FF.snapshots[(Ls * HV, 4, 8)](pool, keys, values, gains, anc_buf, accept_index, ends, slots64[r:r + 1], zero,
+                                      inter, N, accept_index.shape[1], *pool.stride(), *inter.stride(), num_warps=4)
+        pool[:, r].copy_(inter[:, 0].index_select(1, last).squeeze(1))
+        conv_state[:, r].copy_(iw[:, 0].index_select(1, last).squeeze(1))
+
+    def cycle():
+        for r in range(Bt):
+            request(r)
+
+    for _ in range(max(args.warmup, 1)):
+        cycle()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        t0.record(stream)
+        for _ in range(args.steps):
+            cycle()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    return {"impl": "reference-gpu", "value": args.steps / (ms / 1e3), "unit": "cycles/s",
+            "ms_per_step": ms / args.steps, "steps": args.steps, "warmup": args.warmup,
+            "path": "reference Triton/torch GPU code from its installed sources, one request at a time",
+            "clocks": clk.summary()}
 
 
 def main():
@@ -560,11 +833,15 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="reference arm: skip the reference's own GPU path (timed in a child process)")
+    ap.add_argument("--requests", type=int, default=256,
+                    help="config-4 stage: requests split over the GPUs (0 skips the stage)")
     ap.add_argument("--no-attn", dest="attn", action="store_false",
                     help="skip the tree-masked attention stage (reported under stages, outside the cycle)")
     ap.add_argument("--profile", action="store_true", help="only W + K plain cycles (for ncu); prints nothing")
@@ -581,16 +858,21 @@ def main():
         if rank == 0:
             print(json.dumps(run_reference(args)), flush=True)
         return
+    if args.impl == "reference-gpu":
+        print(json.dumps(run_reference_gpu(args)), flush=True)
+        return
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile:
-        # before the first GPU call (spawned workers)
+        # before the first GPU call (spawned workers): one warm-up cycle, then one timed whole cycle
         workers = max(1, min(os.cpu_count() or 1, 64))
-        sampler = CpuSampler(workers)
+        cc = CpuCycle(workers, args.batch, args.layers)
         try:
-            v, sample, _ = sampler.rate(2, 4)
+            cc.cycle()
+            t = cc.cycle()
+            cpu = {"value": 1.0 / t, "unit": "cycles/s", "cores": workers, "kind": cc.kind,
+                   "sample": "one " + cc.describe()[len("whole "):].replace("cycles:", "cycle:", 1)}
         finally:
-            sampler.close()
-        cpu = {"value": v, "unit": "cycles/s", "cores": workers, "kind": "port", "sample": sample}
+            cc.close()
     if world > 1:
         import datetime
 

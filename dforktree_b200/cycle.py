@@ -1,5 +1,6 @@
 """Batched draft-tree cycle on one GPU: score -> build -> (tree conv + GDN
-verify) per GDN layer -> greedy acceptance -> closed-form commit.
+verify) per GDN layer, tree-masked attention per gated full-attention layer
+(in the model's layer order) -> greedy acceptance -> closed-form commit.
 
 This is the B200-native form of what the plugin does per decode step for one
 request (fc1_branch64.verify_branch: Builder at :25, the patched conv and
@@ -13,6 +14,9 @@ State layout in HBM (one GPU holds whole requests; requests shard across GPUs):
   aux_k     [L, B, Hk, N, Dk] fp32    normalised keys saved by verify (per k-head)
   aux_vn    [L, B, Hv, N, Dv] fp32    delta-rule values saved by verify
   aux_g     [L, B, Hv, N]     fp32    ancestor-cumulative gates
+  k_cache / v_cache [La, slots, Hkv, Da] bf16   per attention layer, page size 1:
+            request b's keys are slots kv_indices[kv_indptr[b]:kv_indptr[b+1]],
+            its prefix first and its N tree tokens last
 """
 from __future__ import annotations
 
@@ -36,6 +40,27 @@ class CycleConfig:
     P: int = 24           # longest accepted path kept (draft block)
     lam_a: float = 0.3
     lam_p: float = 0.6
+    chain_first: bool = False   # FC1_CHAIN_FIRST (fc1_builder.py:12): top-1 chain first
+    # gated full-attention layers (Qwen3.5: every 4th layer; 0 = GDN layers only)
+    attn_layers: int = 0
+    Hq: int = 16
+    Hkv: int = 4
+    Da: int = 256
+    prefix: int = 4096    # prior context per request in the KV cache
+
+    @property
+    def layer_kinds(self):
+        """'gdn' / 'attn' per model layer in order: three GDN layers, then one
+        attention layer, repeated (attention layers beyond that pattern last)."""
+        kinds, g, a = [], 0, 0
+        while g < self.layers or a < self.attn_layers:
+            if a < self.attn_layers and (g == self.layers or (len(kinds) + 1) % 4 == 0):
+                kinds.append("attn")
+                a += 1
+            else:
+                kinds.append("gdn")
+                g += 1
+        return kinds
 
     @property
     def C(self):
@@ -80,12 +105,41 @@ class DraftTreeCycle:
         self.pool_out = torch.as_strided(p, (Ls, B, 1, c.Hv, D, D),
                                          (p.stride(0), p.stride(1), 0, p.stride(2), p.stride(3), p.stride(4)))
         self.launches_per_step = 3 + Ls + 1 + 1 + 1
+        if c.attn_layers:
+            self._init_attention(g)
+
+    def _init_attention(self, g):
+        """KV caches of the attention layers (random prefix + tree keys in
+        shuffled page-size-1 slots) and the plan, made once: the plan reads the
+        tree's ancestor matrix from its buffer at every run."""
+        from .tree_attn import TreeAttentionWrapper
+        c, dev = self.cfg, self.device
+        keys = c.prefix + c.N
+        slots = c.B * keys
+        self.kv_indices = torch.randperm(slots, device=dev, generator=g).to(torch.int32)
+        self.kv_indptr = (torch.arange(c.B + 1, device=dev) * keys).to(torch.int32)
+        self.k_cache = torch.empty(c.attn_layers, slots, c.Hkv, c.Da, dtype=torch.bfloat16, device=dev)
+        self.v_cache = torch.empty_like(self.k_cache)
+        for j in range(c.attn_layers):
+            self.k_cache[j] = torch.randn(slots, c.Hkv, c.Da, device=dev, generator=g)
+            self.v_cache[j] = torch.randn(slots, c.Hkv, c.Da, device=dev, generator=g)
+        self.attn = TreeAttentionWrapper(dev).plan(self.kv_indptr, self.kv_indices, c.Hq, c.Hkv, c.Da, n=c.N,
+                                                   anc=self.tree["anc"], kv_lens_host=[keys] * c.B)
+        self.attn.status = self.status
+        self.o_attn = torch.empty(c.B, c.N, c.Hq, c.Da, dtype=torch.bfloat16, device=dev)
+        self.launches_per_step += c.attn_layers * 2
 
     # -- stages --------------------------------------------------------------
     def build(self, logits, root, pre1):
         c = self.cfg
-        K.score_build(self.table, logits, root, pre1, c.N, self.ws, self.tree, lam_a=c.lam_a, lam_p=c.lam_p,
-                      status=self.status)
+        K.score_build(self.table, logits, root, pre1, c.N, self.ws, self.tree, chain_first=c.chain_first,
+                      lam_a=c.lam_a, lam_p=c.lam_p, status=self.status)
+
+    def attend_layer(self, j, q):
+        """Tree-masked attention verify of attention layer j: q [B, N, Hq, Da]
+        against the request's prefix and its tree keys (mask of
+        fc1_branch64.py:39); output in self.o_attn."""
+        return self.attn.run(q, (self.k_cache[j], self.v_cache[j]), out=self.o_attn)
 
     def verify_layer(self, l, x, a, b):
         """Tree conv fused into the GDN tree verify of layer l (one launch).
@@ -121,11 +175,24 @@ class DraftTreeCycle:
         if x is not None:
             K.conv_commit(x, self.conv_state, self.tree["cidx"], self.last, status=self.status)
 
-    def step(self, logits, root, pre1, x, a, b, target_fn):
-        """One cycle.  x [L, B, N, C], a / b [L, B, N, Hv]; target_fn(tree) ->
-        the target model's token per node [B, N] (int64)."""
+    def verify(self, x, a, b, q=None):
+        """Every layer in model order: tree conv + GDN verify per GDN layer
+        (each launch overlapping the previous layer's tail), tree attention
+        per attention layer (q [La, B, N, Hq, Da])."""
+        l = j = 0
+        for kind in self.cfg.layer_kinds:
+            if kind == "gdn":
+                self.verify_layer(l, x[l], a[l], b[l])
+                l += 1
+            else:
+                self.attend_layer(j, q[j])
+                j += 1
+
+    def step(self, logits, root, pre1, x, a, b, target_fn, q=None):
+        """One cycle.  x [L, B, N, C], a / b [L, B, N, Hv]; q [La, B, N, Hq, Da]
+        when the cycle has attention layers; target_fn(tree) -> the target
+        model's token per node [B, N] (int64)."""
         self.build(logits, root, pre1)
-        for l in range(self.cfg.layers):
-            self.verify_layer(l, x[l], a[l], b[l])
+        self.verify(x, a, b, q)
         self.accept(target_fn(self.tree))
         self.commit(x)

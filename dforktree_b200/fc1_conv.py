@@ -42,6 +42,14 @@ def make_hook(original):
     return call
 
 
+_installed = False
+
+
 def install():
+    """Patch SGLang's causal_conv1d_update (fc1_conv.py:29-46); idempotent."""
+    global _installed
+    if _installed:
+        return
     from sglang.srt.layers.attention.linear import gdn_backend as backend
     backend.causal_conv1d_update = make_hook(backend.causal_conv1d_update)
+    _installed = True

@@ -19,6 +19,7 @@ NN = int(os.environ.get("FC1_TREE_N", "64"))
 BS = int(os.environ.get("FC1_DRAFT_BLOCK", "24"))
 CTX = None
 NATIVE_REFERENCE = False
+_installed = False
 
 
 class Context:
@@ -97,7 +98,12 @@ def make_hooks(original_target_verify, original_commit, verify_commit_step_indic
 
 
 def install():
-    """Patch SGLang's GDN verify / commit / routing (fc1_fused.py:53-97)."""
+    """Patch SGLang's GDN verify / commit / routing (fc1_fused.py:53-97).
+    Idempotent: a second call (the reference's register() reaching this module
+    through its bare name) keeps the hooks already installed."""
+    global _installed
+    if _installed:
+        return
     from sglang.srt.layers.attention.linear.kernels.gdn_triton import TritonGDNKernel
     from sglang.srt.speculative import eagle_worker_common as common
     from sglang.srt.speculative.spec_utils import _verify_commit_step_indices
@@ -115,3 +121,15 @@ def install():
     GDNAttnBackend._target_verify_supports_strided_qkv = direct_routing
     TritonGDNKernel.target_verify = fused
     common.commit_mamba_states_after_verify = fused_commit
+    _installed = True
+
+
+def set_tree(anc, cidx):
+    """The tree hand-off of fc1_branch64.py:26-30 as a call: copy the built
+    tree's ancestor matrix [NN, NN] and conv columns [NN, 4] into the hooks'
+    context (created on first use, as the hooks do)."""
+    global CTX
+    if CTX is None:
+        CTX = Context(device=anc.device)
+    CTX.anc.copy_(anc)
+    CTX.cidx.copy_(cidx)

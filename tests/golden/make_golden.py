@@ -11,8 +11,8 @@ The reference modules are imported from their own sources: `ngram_gpu`,
 
 The one piece the reference does not ship -- the closure returned by
 `tree_ops.ngram_path_fn` (tree_ops.py:66 returns an undefined `fn`) -- is
-supplied by `_reconstructed_fn`, which is the reconstruction the oracle and
-the CUDA path implement; the reference's own code computes the PMI tensor T
+supplied by `oracle.reference_shim.reconstructed_fn`, which is the
+reconstruction the oracle and the CUDA path implement; the reference's own code computes the PMI tensor T
 it closes over, the beam search and the tree structure.
 
 Inputs are rebuilt from seeds by `tests/golden/cases.py`; each fixture stores
@@ -32,20 +32,12 @@ import numpy as np  # noqa: E402
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
+from oracle import reference_shim  # noqa: E402
 from tests.golden import cases  # noqa: E402
 
 
 def _load_reference(ref_dir: str):
-    sys.path.insert(0, ref_dir)
-    import torch  # noqa: F401
-    import ngram_gpu  # noqa: F401
-    import tree_ops  # noqa: F401
-    import fc1_builder  # noqa: F401
-    import tree_kernels  # noqa: F401
-    import fc1_block_inverse  # noqa: F401
-    import fc1_fused  # noqa: F401
-    import fc1_conv  # noqa: F401
-    return sys.modules
+    return reference_shim.load_reference(ref_dir)
 
 
 def _table_file(table: dict) -> str:
@@ -55,44 +47,8 @@ def _table_file(table: dict) -> str:
     return path
 
 
-def _reconstructed_fn(T, lp, rest, lam_a, lam_p):
-    """Fork-aware closure (reconstruction; see oracle/builder.py)."""
-    import torch
-
-    def fn(s, cand, pc, ppc, al):
-        t = T[s - 1][pc, cand]
-        lam = torch.where(al, lam_a, lam_p)[:, None].to(t.dtype)
-        x = lp[s][None, :] + lam * t
-        r = rest[s].reshape(1, 1).expand(x.shape[0], 1)
-        return x - torch.logsumexp(torch.cat((x, r), -1), -1, keepdim=True)
-
-    return fn
-
-
 def _patch_path_fn(mods):
-    """Wrap tree_ops.ngram_path_fn: let the reference build T, then return the
-    reconstructed closure over it (the shipped function ends in NameError)."""
-    TO = mods["tree_ops"]
-    original = TO.ngram_path_fn
-    captured = {}
-
-    class _Capture:
-        def __init__(self, ng):
-            self.ng = ng
-
-        def pmi(self, *args):
-            out = self.ng.pmi(*args)
-            captured["T"] = out.float()
-            return out
-
-    def patched(ng, order, ids, lp, rest, pre1, root, lam_a, lam_p):
-        TO.fn = None  # the name `fn` that the shipped function returns
-        original(_Capture(ng), order, ids, lp, rest, pre1, root, lam_a, lam_p)
-        del TO.fn
-        return _reconstructed_fn(captured["T"], lp, rest, lam_a, lam_p)
-
-    TO.ngram_path_fn = patched
-    return captured
+    return reference_shim.patch_path_fn(mods)
 
 
 def gen_ngram(mods, out_dir):

@@ -1,0 +1,146 @@
+"""The cycle bench.py times, at its exact configuration, against the oracle.
+
+64 requests x S = 24 positions over V = 248,320 fp32 logits with the
+2M-bigram + 8M-trigram table, 24 GDN layers of the Qwen3.5-9B shape (tree conv
+fused into the tcgen05 verifier, consecutive layers overlapped by
+programmatic dependent launch, one shared output buffer), greedy acceptance
+along the deepest node's path for a drawn length, in-place commit of every
+layer's state and conv window -- the same inputs (dforktree_b200.workload) and
+the same calls as bench.py's timed step.  Four requests spread over the batch
+are recomputed on the CPU:
+
+* trees (tokens, parents, depth, ancestors, conv columns, nxt / sib)
+  bit-exact, a difference accepted only as a classified fp32 score tie;
+* the accepted path equals the host restatement of the target stand-in;
+* layers 0 and 23: verify outputs o within 2e-2 (bf16 activations),
+  normalised keys / delta-rule values / gates within 1e-3, committed states
+  of all 32 heads within 1e-3 relative to their largest magnitude, and the
+  committed conv windows exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import builder as OB
+from oracle import gdn as OG
+from oracle import ngram as ON
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+SAMPLE = (0, 21, 42, 63)
+CHECK_LAYERS = (0, 23)
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _rel(a, b):
+    return float(np.abs(np.asarray(a, np.float64) - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def _tie_gap(trace, W, N):
+    gaps = []
+    for t in trace[:-1] + [trace[-1][:N]]:
+        t = t[: W + 1]
+        t = t[np.isfinite(t)]
+        if t.size > 1:
+            gaps.append(np.min(np.abs(np.diff(t)) / np.maximum(np.abs(t[:-1]), 1.0)))
+    return min(gaps) if gaps else np.inf
+
+
+@pytest.fixture(scope="module")
+def bench_cycle():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from dforktree_b200 import build
+    build.build()
+    import bench
+    from dforktree_b200 import kernels as K
+    from dforktree_b200 import synth
+    from dforktree_b200 import workload as WL
+    from dforktree_b200.cycle import CycleConfig, DraftTreeCycle
+    from dforktree_b200.ngram_gpu import load_npz_arrays
+
+    torch.cuda.set_device(0)
+    table_np = synth.make_ngram_table(bench.V, 2_000_000, 8_000_000, seed=0)
+    table = K.Table(load_npz_arrays(table_np), beta3=60.0, device=DEV)
+    cfg = CycleConfig(B=64, layers=bench.LAYERS)
+    assert (cfg.S, cfg.V, cfg.N, cfg.Hk, cfg.Hv, cfg.D) == (bench.S, bench.V, bench.N, bench.HK, bench.HV, bench.D)
+    cyc = DraftTreeCycle(cfg, table, DEV, seed=0)
+    inp = WL.cycle_inputs(cfg, DEV, seed=1234)
+    idx = torch.tensor(SAMPLE, device=DEV)
+    lidx = torch.tensor(CHECK_LAYERS, device=DEV)
+    before = dict(pool=_np(cyc.pool.index_select(0, lidx).index_select(1, idx)),
+                  conv_state=_np(cyc.conv_state.index_select(0, lidx).index_select(1, idx)))
+    x, a, b = inp["x"], inp["a"], inp["b"]
+    # bench.py's timed step (DraftTreeCycle.step), keeping layers 0 / 23's outputs
+    o_keep = {}
+    cyc.build(inp["logits"], inp["root"], inp["pre1"])
+    for l in range(cfg.layers):
+        cyc.verify_layer(l, x[l], a[l], b[l])
+        if l in CHECK_LAYERS:
+            o_keep[l] = cyc.o.index_select(0, idx).clone()
+    cyc.accept(WL.path_target(cyc.tree, inp["acc_len"]))
+    cyc.commit(x)
+    torch.cuda.synchronize()
+    return dict(cyc=cyc, inp=inp, table_np=table_np, before=before, o=o_keep, idx=idx, lidx=lidx)
+
+
+def test_bench_cycle_device_status(bench_cycle):
+    assert int(bench_cycle["cyc"].status.item()) == 0
+
+
+def test_bench_cycle_trees_match_oracle(bench_cycle):
+    cyc, inp = bench_cycle["cyc"], bench_cycle["inp"]
+    ong = ON.NGramOracle(bench_cycle["table_np"], beta3=60.0)
+    keys = ("tokens", "parent", "depth", "anc", "cidx", "nxt", "sib")
+    for r in SAMPLE:
+        trace = []
+        tr = OB.builder_run(_np(inp["logits"][r]), int(inp["root"][r]), int(inp["pre1"][r]), ong, N=32, trace=trace)
+        bad = [k for k in keys if not np.array_equal(cyc.tree[k][r].cpu().numpy(), np.asarray(tr[k]))]
+        if bad:
+            gap = _tie_gap(trace, 31, 32)
+            assert gap < 1e-5, f"request {r}: tree differs in {bad} (no fp32 tie: gap {gap:.2e})"
+
+
+def test_bench_cycle_accepted_paths(bench_cycle):
+    from dforktree_b200 import workload as WL
+    cyc, inp = bench_cycle["cyc"], bench_cycle["inp"]
+    for r in SAMPLE:
+        t = {k: cyc.tree[k][r].cpu().numpy() for k in ("parent", "depth", "anc")}
+        p = WL.expected_path(t["parent"], t["depth"], t["anc"], int(inp["acc_len"][r]))
+        got = cyc.path[r].cpu().numpy()
+        assert list(got[: len(p)]) == p and np.all(got[len(p):] == -1), r
+        assert int(cyc.accept_len[r]) == len(p) and int(cyc.last[r]) == p[-1]
+
+
+@pytest.mark.parametrize("li", range(len(CHECK_LAYERS)))
+def test_bench_cycle_layer_outputs_and_commit(bench_cycle, li):
+    cyc, inp = bench_cycle["cyc"], bench_cycle["inp"]
+    cfg = cyc.cfg
+    l = CHECK_LAYERS[li]
+    o_gpu = _np(bench_cycle["o"][l])
+    pool0 = bench_cycle["before"]["pool"][li]            # [4, Hv, Dv, Dk]
+    cs0 = bench_cycle["before"]["conv_state"][li]        # [4, C, 3]
+    for i, r in enumerate(SAMPLE):
+        anc = cyc.tree["anc"][r].cpu().numpy()
+        cidx = cyc.tree["cidx"][r].cpu().numpy()
+        path = cyc.path[r].cpu().numpy()
+        last = int(cyc.last[r])
+        xr = _np(inp["x"][l, r])
+        y, _ = OG.tree_conv(xr, cs0[i], _np(cyc.conv_w[l]), None, cidx)
+        y = _np(torch.from_numpy(y).to(torch.bfloat16))      # the fused conv output is rounded to x's dtype
+        o, k, vn, G = OG.tree_gdn(y, _np(inp["a"][l, r]), _np(inp["b"][l, r]), _np(cyc.A_log[l]),
+                                  _np(cyc.dt_bias[l]), pool0, i, anc, cfg.Hk, cfg.Hv, cfg.D, cfg.D)
+        assert _rel(o_gpu[i], o) < 2e-2, (l, r)
+        assert _rel(_np(cyc.aux_vn[l, r]), vn) < 1e-3, (l, r)
+        # k-hat is stored once per k-head (aux_k_per_v=False): v-head h uses k-head h // 2
+        assert _rel(_np(cyc.aux_k[l, r]), k[:: cfg.Hv // cfg.Hk]) < 1e-3, (l, r)
+        np.testing.assert_allclose(_np(cyc.aux_g[l, r]), G, rtol=1e-5, atol=1e-5)
+        for h in range(cfg.Hv):
+            ref = OG.snapshot(pool0[i, h], k[h], vn[h], G[h], anc, path, last)
+            assert _rel(_np(cyc.pool[l, r, h]), ref) < 1e-3, (l, r, h)
+        cols = cidx[last, 1:]
+        win = np.stack([cs0[i][:, c] if c < 3 else xr[c - 3] for c in cols], 1)
+        np.testing.assert_array_equal(_np(cyc.conv_state[l, r]), win)
