@@ -144,3 +144,42 @@ def commit_inputs(case: dict):
 def checksum(*arrays) -> np.ndarray:
     """float64 sums of each array (detects generator drift)."""
     return np.array([float(np.asarray(a, np.float64).sum()) for a in arrays], np.float64)
+
+
+# ------------------------------------------------------ tree attention ------
+# flashinfer's paged prefill (fa2, page size 1) with the plugin's custom mask
+# (fc1_branch64.py:39), one request per plan as fc1_plan.py:16-33 plans it.
+# Grouped-query ratios 1/2/4/8, ragged prefixes, trees of 16 and 32 nodes.
+ATTN_CASES = [
+    dict(name="attn_g4_n32", Hq=16, Hkv=4, N=32, prefixes=[700, 45], seed=400),
+    dict(name="attn_g2_n32", Hq=8, Hkv=4, N=32, prefixes=[128, 1000, 7], seed=401),
+    dict(name="attn_g1_n16", Hq=4, Hkv=4, N=16, prefixes=[300], seed=402),
+    dict(name="attn_g8_n16", Hq=16, Hkv=2, N=16, prefixes=[513, 64], seed=403),
+]
+ATTN_D = 256
+
+
+def _bf16(x: np.ndarray) -> np.ndarray:
+    """Round float32 to the nearest bfloat16 (ties to even), kept as float32."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def attn_inputs(case):
+    """q [B, N, Hq, D]; k / v caches [slots, Hkv, D] (bf16 values as float32);
+    request b's keys are kv_indices[kv_indptr[b]:kv_indptr[b+1]] in shuffled
+    slots, its prefix first and its N tree nodes last; anc [B, N, N] of random
+    trees (config-2 topology)."""
+    rng = np.random.default_rng(case["seed"])
+    N, Hq, Hkv, D = case["N"], case["Hq"], case["Hkv"], ATTN_D
+    lens = [p + N for p in case["prefixes"]]
+    B, total = len(lens), sum(lens)
+    slots = total + 13
+    kv_indices = rng.permutation(slots)[:total].astype(np.int32)
+    kv_indptr = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    anc = np.stack([synth.ancestors_from_parents(synth.random_tree_parents(N, rng)) for _ in range(B)])
+    q = _bf16(rng.standard_normal((B, N, Hq, D), dtype=np.float32))
+    k = _bf16(rng.standard_normal((slots, Hkv, D), dtype=np.float32))
+    v = _bf16(rng.standard_normal((slots, Hkv, D), dtype=np.float32))
+    return dict(q=q, k=k, v=v, kv_indptr=kv_indptr, kv_indices=kv_indices, anc=anc)

@@ -180,3 +180,26 @@ def test_tree_attention_matches_flashinfer_custom_mask():
         ref = w.run(c["q"][b], (c["k"].unsqueeze(1), c["v"].unsqueeze(1)))
         torch.cuda.synchronize()
         assert _rel(ours[b], _np(ref)) < TOL, (b, _rel(ours[b], _np(ref)))
+
+
+@pytest.mark.parametrize("case", __import__("tests.golden.cases", fromlist=["ATTN_CASES"]).ATTN_CASES,
+                         ids=lambda c: c["name"])
+def test_tree_attention_matches_flashinfer_golden(case):
+    """dft_tree_attn against flashinfer's own paged prefill output (fa2, page
+    size 1, the fc1_branch64.py:39 mask, planned as fc1_plan.py:16-33 plans it;
+    fixtures from tests/golden/make_attn_golden.py), GQA ratios 1 / 2 / 4 / 8,
+    ragged prefixes, N = 16 and 32; bf16 bar 2e-2."""
+    import os
+
+    from tests.golden import cases
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", case["name"] + ".npz"))
+    d = cases.attn_inputs(case)
+    t = lambda x: torch.from_numpy(x).to(DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    from dforktree_b200 import kernels as K
+    o = K.tree_attention(t(d["q"]).to(torch.bfloat16), t(d["k"]).to(torch.bfloat16), t(d["v"]).to(torch.bfloat16),
+                         t(d["kv_indptr"]), t(d["kv_indices"]), t(d["anc"]), status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    ref = (g["o_bf16"].astype(np.uint32) << 16).view(np.float32)
+    assert _rel(_np(o), ref) < TOL

@@ -141,3 +141,19 @@ def test_commit_closed_form_equals_recurrence():
         s = gdn.snapshot(d["pool"][case["slot"], h], k[h], vn[h], G[h], d["anc"], d["path"], u)
         ref = S[h, u].T
         assert np.abs(s - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("case", cases.ATTN_CASES, ids=lambda c: c["name"])
+def test_attention_oracle_matches_flashinfer_golden(case):
+    """oracle/attn.py against flashinfer's own paged prefill (fa2, page size 1,
+    the plugin's custom mask, one request per plan as fc1_plan.py plans it),
+    fixtures written by tests/golden/make_attn_golden.py.  flashinfer rounds P
+    to bf16 before P.V and its output to bf16; the fp32 restatement agrees
+    within 1e-2 of the largest magnitude."""
+    from oracle import attn as OA
+    g = np.load(os.path.join(GOLD, case["name"] + ".npz"))
+    d = cases.attn_inputs(case)
+    np.testing.assert_allclose(g["checksum"], cases.checksum(d["q"], d["k"], d["v"], d["kv_indices"], d["anc"]))
+    ref = (g["o_bf16"].astype(np.uint32) << 16).view(np.float32)
+    o = OA.tree_attention(d["q"], d["k"], d["v"], d["kv_indptr"], d["kv_indices"], d["anc"])
+    assert np.abs(o - ref).max() <= 1e-2 * np.abs(ref).max()
