@@ -168,12 +168,19 @@ __device__ __forceinline__ unsigned long long slot_key(uint4 v) {
   return (static_cast<unsigned long long>(v.y) << 32) | v.x;
 }
 
-// Device view of the n-gram tables (POD, passed by value).
+// Device view of the n-gram tables (POD, passed by value).  Each slot array
+// has a fingerprint array beside it, one byte per slot: 0 for an empty slot,
+// else fp_of(mix64(key)) (never 0).  The fingerprints are small enough to stay
+// in L2 (1/16 of the slots' bytes), so a probe that misses -- the common case
+// for drafted candidates -- resolves there without reading the slot in HBM.
 struct TableView {
   int64_t V;
   const Slot* pair; unsigned long long pair_mask;
   const Slot* trip; unsigned long long trip_mask;
   const Slot* quad; unsigned long long quad_mask;
+  const uint8_t* pair_fp;
+  const uint8_t* trip_fp;
+  const uint8_t* quad_fp;
   const float* prev;
   const float* pn;
   const float* n4c;
@@ -181,8 +188,57 @@ struct TableView {
   float beta2, beta3, beta4, clip;
 };
 
+// Fingerprint of a key from the high bits of its hash (the bucket index uses
+// the low bits): 1..255, 0 marks an empty slot.
+__host__ __device__ __forceinline__ uint32_t fp_of(unsigned long long h) { return 1u + (uint32_t)(h >> 56) % 255u; }
+
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// the aligned 8 fingerprints around a slot (kept in L2: evict-last)
+__device__ __forceinline__ uint2 ld_fp8(const uint8_t* p, uint64_t pol) {
+  uint2 r;
+  asm volatile("ld.global.nc.L2::cache_hint.v2.u32 {%0, %1}, [%2], %3;" : "=r"(r.x), "=r"(r.y) : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ uint32_t fp_byte(uint2 w, int k) { return ((k < 4 ? w.x : w.y) >> (8 * (k & 3))) & 0xFFu; }
+
+// Probe with fingerprints from bucket `idx` on (fingerprint f of key q):
+// fingerprint bytes decide emptiness and candidates; only a candidate's slot
+// is read.  Returns the matching slot or a zero slot.
+static __device__ __noinline__ uint4 probe_fp_from(const Slot* tab, const uint8_t* fp, unsigned long long mask,
+                                            unsigned long long uq, uint32_t f, unsigned long long idx,
+                                            int32_t* status) {
+  const uint64_t pol = l2_evict_last_policy();
+  for (unsigned long long n = 0; n <= mask;) {
+    const uint2 w = ld_fp8(fp + (idx & ~7ull), pol);
+    for (int k = (int)(idx & 7); k < 8 && n <= mask; ++k, ++n) {
+      const uint32_t b = fp_byte(w, k);
+      const unsigned long long at = (idx & ~7ull) + k;
+      if (b == 0) return make_uint4(0, 0, 0, 0);
+      if (b == f) {
+        const uint4 s = __ldg(reinterpret_cast<const uint4*>(tab + at));
+        if (((static_cast<unsigned long long>(s.y) << 32) | s.x) == uq) return s;
+      }
+    }
+    idx = ((idx & ~7ull) + 8) & mask;
+  }
+  raise_status(status, DFT_DEV_PROBE_LIMIT);
+  return make_uint4(0, 0, 0, 0);
+}
+
 // Probe an open-addressed table; returns the matching slot (key == q) or a
 // zero slot on a miss.  Negative keys never match (table keys are >= 0).
+// With fingerprints (fp != nullptr) the slots are read only on a fingerprint match.
+__device__ __forceinline__ uint4 probe_fp(const Slot* tab, const uint8_t* fp, unsigned long long mask, long long q,
+                                          int32_t* status) {
+  if (q < 0 || tab == nullptr) return make_uint4(0, 0, 0, 0);
+  const unsigned long long uq = static_cast<unsigned long long>(q), h = mix64(uq);
+  return probe_fp_from(tab, fp, mask, uq, fp_of(h), h & mask, status);
+}
+
 __device__ __forceinline__ uint4 probe(const Slot* tab, unsigned long long mask, long long q,
                                        int32_t* status) {
   uint4 z = make_uint4(0, 0, 0, 0);

@@ -22,6 +22,9 @@ struct dft_table {
   Slot* pair = nullptr;
   Slot* trip = nullptr;
   Slot* quad = nullptr;
+  uint8_t* pair_fp = nullptr;   // one fingerprint byte per slot (derived: rebuilt on create and load)
+  uint8_t* trip_fp = nullptr;
+  uint8_t* quad_fp = nullptr;
   float* prev = nullptr;
   float* pn = nullptr;
   float* n4c = nullptr;
@@ -81,6 +84,23 @@ __global__ void insert_keys(Slot* tab, unsigned long long mask, const int64_t* _
   atomicOr(err, kErrFull);
 }
 
+// fingerprint byte of every slot (0 = empty)
+__global__ void build_fingerprints(const Slot* tab, uint8_t* fp, int64_t n) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i < n) {
+    const unsigned long long k = tab[i].key;
+    fp[i] = k == kEmptyKey ? 0 : (uint8_t)fp_of(mix64(k));
+  }
+}
+
+int alloc_fingerprints(const Slot* tab, uint8_t** fp, int64_t slots, cudaStream_t st) {
+  if (!slots) return DFT_OK;
+  DFT_CUDA_CHECK(cudaMalloc(fp, (size_t)slots));
+  build_fingerprints<<<(unsigned)((slots + 255) / 256), 256, 0, st>>>(tab, *fp, slots);
+  DFT_LAUNCH_CHECK();
+  return DFT_OK;
+}
+
 int64_t pow2_at_least(double x) {
   int64_t c = 1024;
   while ((double)c < x) c <<= 1;
@@ -106,7 +126,7 @@ int insert(Slot* tab, int64_t slots, const int64_t* keys, const float* vals, int
 // Device view and byte count of a table whose arrays are in place.
 void set_view(dft_table* t, int64_t V, bool has_trip, bool has_quad, bool has_ctx, float beta2, float beta3,
               float beta4, float clip) {
-  t->bytes = (t->pair_slots + t->trip_slots + t->quad_slots) * (int64_t)sizeof(Slot) +
+  t->bytes = (t->pair_slots + t->trip_slots + t->quad_slots) * (int64_t)(sizeof(Slot) + 1) +
              2 * V * (int64_t)sizeof(float) + t->n4c_len * (int64_t)sizeof(float);
   TableView& v = t->view;
   v.V = V;
@@ -116,6 +136,9 @@ void set_view(dft_table* t, int64_t V, bool has_trip, bool has_quad, bool has_ct
   v.trip_mask = t->trip_slots ? (unsigned long long)(t->trip_slots - 1) : 0ull;
   v.quad = t->quad;
   v.quad_mask = t->quad_slots ? (unsigned long long)(t->quad_slots - 1) : 0ull;
+  v.pair_fp = t->pair_fp;
+  v.trip_fp = t->trip_fp;
+  v.quad_fp = t->quad_fp;
   v.prev = t->prev;
   v.pn = t->pn;
   v.n4c = t->n4c;
@@ -134,6 +157,9 @@ void free_table(dft_table* t) {
   cudaFree(t->pair);
   cudaFree(t->trip);
   cudaFree(t->quad);
+  cudaFree(t->pair_fp);
+  cudaFree(t->trip_fp);
+  cudaFree(t->quad_fp);
   cudaFree(t->prev);
   cudaFree(t->pn);
   cudaFree(t->n4c);
@@ -202,6 +228,11 @@ extern "C" int dft_table_create(const dft_table_desc* d, dft_table** out, void* 
     }
   }
   cudaFree(err);
+  err = nullptr;
+  TRY(alloc_fingerprints(t->pair, &t->pair_fp, t->pair_slots, st));
+  TRY(alloc_fingerprints(t->trip, &t->trip_fp, t->trip_slots, st));
+  TRY(alloc_fingerprints(t->quad, &t->quad_fp, t->quad_slots, st));
+  TRY(cudaStreamSynchronize(st) == cudaSuccess ? DFT_OK : DFT_ERR_CUDA);
   t->n4c_len = d->n_quad ? d->n_trigram : 0;
   set_view(t, d->V, d->n_trigram > 0, d->n_quad > 0, d->n_ctx3 > 0, d->beta2, d->beta3, d->beta4, d->clip);
   *out = t;
@@ -475,6 +506,10 @@ extern "C" int dft_table_load(const char* path, dft_table** out, void* stream) {
   if (rc == DFT_OK && (sum != h.checksum || fread(&extra, 1, 1, f) != 0)) rc = DFT_ERR_IO;
   fclose(f);
   if (cudaStreamSynchronize(st) != cudaSuccess && rc == DFT_OK) rc = DFT_ERR_CUDA;
+  if (rc == DFT_OK) rc = alloc_fingerprints(t->pair, &t->pair_fp, t->pair_slots, st);
+  if (rc == DFT_OK) rc = alloc_fingerprints(t->trip, &t->trip_fp, t->trip_slots, st);
+  if (rc == DFT_OK) rc = alloc_fingerprints(t->quad, &t->quad_fp, t->quad_slots, st);
+  if (rc == DFT_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = DFT_ERR_CUDA;
   if (rc != DFT_OK) {
     free_table(t);
     return rc;
@@ -499,7 +534,7 @@ __device__ __forceinline__ float prev_at(const TableView& t, long long b, int32_
 }
 
 __device__ float p2_query(const TableView& t, long long b, long long c, int32_t* st) {
-  uint4 s = probe(t.pair, t.pair_mask, b * t.V + c, st);
+  uint4 s = probe_fp(t.pair, t.pair_fp, t.pair_mask, b * t.V + c, st);
   return p2_from(__uint_as_float(s.z), prev_at(t, b, st), pn_at(t, c, st), t.beta2);
 }
 
@@ -508,8 +543,8 @@ __device__ float p3_query(const TableView& t, long long a, long long b, long lon
   long long V = t.V;
   float nab = 0.f, nabc = 0.f;
   if (ok) {
-    if (t.has_ctx) nab = __uint_as_float(probe(t.pair, t.pair_mask, a * V + b, st).w);
-    if (t.has_trip) nabc = __uint_as_float(probe(t.trip, t.trip_mask, (a * V + b) * V + c, st).z);
+    if (t.has_ctx) nab = __uint_as_float(probe_fp(t.pair, t.pair_fp, t.pair_mask, a * V + b, st).w);
+    if (t.has_trip) nabc = __uint_as_float(probe_fp(t.trip, t.trip_fp, t.trip_mask, (a * V + b) * V + c, st).z);
   }
   return p3_from(nabc, nab, p2_query(t, b, c, st), t.beta3);
 }
@@ -519,12 +554,12 @@ __device__ float p4_query(const TableView& t, long long z, long long a, long lon
   long long V = t.V;
   float n4 = 0.f, c4 = 0.f;
   if (ok && t.has_trip) {
-    uint4 s = probe(t.trip, t.trip_mask, (z * V + a) * V + b, st);
+    uint4 s = probe_fp(t.trip, t.trip_fp, t.trip_mask, (z * V + a) * V + b, st);
     if (slot_key(s) == static_cast<unsigned long long>((z * V + a) * V + b)) {
       long long i3 = (long long)s.w;
       if (t.has_quad) {
         n4 = __ldg(t.n4c + i3);
-        c4 = __uint_as_float(probe(t.quad, t.quad_mask, i3 * V + c, st).z);
+        c4 = __uint_as_float(probe_fp(t.quad, t.quad_fp, t.quad_mask, i3 * V + c, st).z);
       }
     }
   }
@@ -549,12 +584,43 @@ __global__ void ngram_eval_kernel(TableView t, int order, int what, const int64_
   out[i] = what ? pmi_from(p, logf(pn_at(t, cc, st)), t.clip) : p;
 }
 
+// Fingerprint probing in two rounds for many independent queries: round 1
+// loads the 8 fingerprints around each query's bucket (L2-resident), round 2
+// scans them -- an empty byte ends a miss, a matching byte names a candidate
+// slot, which is then read from HBM and compared.  A false candidate or a
+// chain longer than the loaded word continues in probe_fp_from.
+__device__ __forceinline__ uint2 fp_round1(const uint8_t* fp, unsigned long long mask, long long q, uint64_t pol) {
+  if (q < 0 || fp == nullptr) return make_uint2(0u, 0u);   // scans as an empty bucket: no match
+  return ld_fp8(fp + ((mix64(static_cast<unsigned long long>(q)) & mask) & ~7ull), pol);
+}
+
+__device__ __forceinline__ uint4 fp_round2(const Slot* tab, const uint8_t* fp, unsigned long long mask, long long q,
+                                           uint2 w, int32_t* st) {
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  if (q < 0 || tab == nullptr) return z;
+  const unsigned long long uq = static_cast<unsigned long long>(q), h = mix64(uq), idx = h & mask;
+  const uint32_t f = fp_of(h);
+  for (int k = (int)(idx & 7); k < 8; ++k) {
+    const uint32_t b = fp_byte(w, k);
+    if (b == 0) return z;
+    if (b == f) {
+      const unsigned long long at = (idx & ~7ull) + k;
+      const uint4 s = ldg_slot(tab + at);
+      if (slot_key(s) == uq) return s;
+      return probe_fp_from(tab, fp, mask, uq, f, (at + 1) & mask, st);
+    }
+  }
+  return probe_fp_from(tab, fp, mask, uq, f, ((idx & ~7ull) + 8) & mask, st);
+}
+
 // Dense PMI tensor for one (request, step t): T[i, j, l] = PMI(a_i, b_j, c_l)
 // with a = E[t+1], b = E[t+2] = ids[t], c = ids[t+1] and E = [pre1; root; ids]
 // (tree_ops.py:56-62, order 3).  256 threads: phase 1 resolves the 256
 // context pairs (a_i, b_j) and 256 bigram pairs (b_j, c_l) in the pair table
-// into shared memory; phase 2 issues 16 independent triple probes per thread
-// (first-slot loads all in flight) and writes T coalesced.
+// into shared memory; phase 2 resolves the 16 x 16 x 16 triples, 16 per
+// thread with every first fingerprint load in flight, and writes T coalesced.
+// At t = 0 every a_i is the root: one row of triples is probed and written 16
+// times.
 constexpr int kM = 16;
 
 __global__ void __launch_bounds__(256) pmi_dense_kernel(TableView t, int S, const int32_t* __restrict__ ids,
@@ -574,6 +640,7 @@ __global__ void __launch_bounds__(256) pmi_dense_kernel(TableView t, int S, cons
   }
   __syncthreads();
   const long long V = t.V;
+  const uint64_t pol = l2_evict_last_policy();
   {
     // context pair (a_i, b_j) and bigram pair (b_j, c_l), one each per thread
     int i = tid >> 4, j = tid & 15;
@@ -582,35 +649,44 @@ __global__ void __launch_bounds__(256) pmi_dense_kernel(TableView t, int S, cons
     int jj = tid >> 4, l = tid & 15;
     long long b2 = sb[jj], c2 = sc[l];
     long long qbig = b2 * V + c2;
-    uint4 s1 = first_slot(t.pair, t.pair_mask, qctx);
-    uint4 s2 = first_slot(t.pair, t.pair_mask, qbig);
+    const uint2 w1 = fp_round1(t.pair_fp, t.pair_mask, qctx, pol);
+    const uint2 w2 = fp_round1(t.pair_fp, t.pair_mask, qbig, pol);
     float pnc = pn_at(t, c2, st);
     float prevb = prev_at(t, b2, st);
-    s1 = probe_from(t.pair, t.pair_mask, qctx, s1, st);
-    s2 = probe_from(t.pair, t.pair_mask, qbig, s2, st);
+    const uint4 s1 = fp_round2(t.pair, t.pair_fp, t.pair_mask, qctx, w1, st);
+    const uint4 s2 = fp_round2(t.pair, t.pair_fp, t.pair_mask, qbig, w2, st);
     s_nab[tid] = __uint_as_float(s1.w);
     s_p2[tid] = p2_from(__uint_as_float(s2.z), prevb, pnc, t.beta2);
     if (jj == 0) s_lpn[l] = logf(pnc);
   }
   __syncthreads();
   float* Tout = T + ((int64_t)req * (S - 1) + tstep) * (kM * kM * kM);
+  const int rows = tstep == 0 ? 1 : 16;       // row r of this thread's triples is i = r
   long long q[16];
-  uint4 s[16];
+  uint2 w[16];
 #pragma unroll
   for (int r = 0; r < 16; ++r) {
     int e = tid + 256 * r;
     int i = e >> 8, j = (e >> 4) & 15, l = e & 15;
     long long a = sa[i], b = sb[j];
-    q[r] = (a >= 0 && b >= 0 && t.has_trip) ? (a * V + b) * V + sc[l] : -1;
-    s[r] = first_slot(t.trip, t.trip_mask, q[r]);
+    q[r] = (r < rows && a >= 0 && b >= 0 && t.has_trip) ? (a * V + b) * V + sc[l] : -1;
+    w[r] = fp_round1(t.trip_fp, t.trip_mask, q[r], pol);
   }
+  float v0 = 0.f;
 #pragma unroll
   for (int r = 0; r < 16; ++r) {
     int e = tid + 256 * r;
     int i = e >> 8, j = (e >> 4) & 15, l = e & 15;
-    uint4 hit = probe_from(t.trip, t.trip_mask, q[r], s[r], st);
-    float p3 = p3_from(__uint_as_float(hit.z), s_nab[i * 16 + j], s_p2[j * 16 + l], t.beta3);
-    Tout[e] = pmi_from(p3, s_lpn[l], t.clip);
+    float v;
+    if (r < rows) {
+      const uint4 hit = fp_round2(t.trip, t.trip_fp, t.trip_mask, q[r], w[r], st);
+      const float p3 = p3_from(__uint_as_float(hit.z), s_nab[i * 16 + j], s_p2[j * 16 + l], t.beta3);
+      v = pmi_from(p3, s_lpn[l], t.clip);
+      if (r == 0) v0 = v;
+    } else {
+      v = v0;   // t = 0: row i equals row 0
+    }
+    Tout[e] = v;
   }
 }
 
