@@ -44,7 +44,7 @@ class TableDesc(C.Structure):
 
 class BuildParams(C.Structure):
     _fields_ = [("B", i32), ("S", i32), ("V", i32), ("M", i32), ("N", i32), ("lmax", i32),
-                ("chain_first", i32), ("use_ngram", i32), ("lam_a", f32), ("lam_p", f32)]
+                ("chain_first", i32), ("use_ngram", i32), ("lam_a", f32), ("lam_p", f32), ("pmi_order", i32)]
 
 
 class TreeOut(C.Structure):

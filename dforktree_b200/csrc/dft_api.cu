@@ -41,6 +41,7 @@ extern "C" int dft_score_build(const dft_table* table, const dft_build_params* p
   if (rc) return rc;
   if (!logits || !root || !workspace || !out) return DFT_ERR_INVALID;
   if (p->use_ngram && !table) return DFT_ERR_INVALID;
+  if (p->use_ngram && dft::pmi_order_of(p) == 4 && !pre1) return DFT_ERR_INVALID;
   if (!dft::valid_dtype(logits_dtype)) return DFT_ERR_INVALID;
   if (ld_s < p->V || ld_b < (int64_t)p->S * ld_s - (ld_s - p->V)) return DFT_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

@@ -41,7 +41,7 @@ __device__ __forceinline__ float half_lse(float x, float extra) {
 }
 
 struct SmemLayout {
-  size_t lp, rest, sc, key, lv, cand, pc, al, fl, csc, clv, cfl, sk, si, K, Pb, Cb, Fb, inv, total;
+  size_t lp, rest, sc, key, lv, cand, pc, ppc, al, fl, csc, clv, cfl, sk, si, K, Pb, Cb, Fb, inv, total;
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
@@ -56,6 +56,7 @@ __host__ __device__ inline SmemLayout smem_layout(int S, int W, int P) {
   L.lv = o; o = align16(o + sizeof(int) * W);
   L.cand = o; o = align16(o + sizeof(int) * W);
   L.pc = o; o = align16(o + sizeof(int) * W);
+  L.ppc = o; o = align16(o + sizeof(int) * W);
   L.al = o; o = align16(o + sizeof(int) * W);
   L.fl = o; o = align16(o + sizeof(int) * W);
   L.csc = o; o = align16(o + sizeof(float) * P);
@@ -73,7 +74,7 @@ __host__ __device__ inline SmemLayout smem_layout(int S, int W, int P) {
 }
 
 struct BeamArgs {
-  int B, S, N, W, lmax, chain_first, use_ngram;
+  int B, S, N, W, lmax, chain_first, use_ngram, order;
   float lam_a, lam_p;
   const float* lp;
   const int32_t* ids;
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(P) beam_kernel(BeamArgs a) {
   int* s_lv = (int*)(smem + Ly.lv);
   int* s_cand = (int*)(smem + Ly.cand);
   int* s_pc = (int*)(smem + Ly.pc);
+  int* s_ppc = (int*)(smem + Ly.ppc);
   int* s_al = (int*)(smem + Ly.al);
   int* s_fl = (int*)(smem + Ly.fl);
   float* c_sc = (float*)(smem + Ly.csc);
@@ -164,6 +166,7 @@ __global__ void __launch_bounds__(P) beam_kernel(BeamArgs a) {
       s_cand[w] = cand;
       s_al[w] = al;
       s_pc[w] = 0;
+      s_ppc[w] = 0;
       s_key[w] = key;
       K[w] = key;
       Pb[w] = 255;
@@ -182,7 +185,12 @@ __global__ void __launch_bounds__(P) beam_kernel(BeamArgs a) {
     const int ww = valid ? w : 0;
     const int cand = s_cand[ww];
     if (a.use_ngram) {
-      const float t = a.T[(((int64_t)b * (S - 1) + (s - 1)) * kM * kM + s_pc[ww] * kM + cand) * kM + l];
+      // the closure's context: cand, pc and ppc are the candidates at
+      // positions s-1, s-2 and s-3 of the beam's path (tree_ops.py:28, 40)
+      int64_t row = (int64_t)b * (S - 1) + (s - 1);
+      if (a.order >= 4) row = row * kM + s_ppc[ww];
+      if (a.order >= 3) row = row * kM + s_pc[ww];
+      const float t = a.T[(row * kM + cand) * kM + l];
       const float lam = s_al[ww] ? a.lam_a : a.lam_p;
       x = __fadd_rn(s_lp[s * kM + l], __fmul_rn(lam, t));
     } else if (!a.logc) {
@@ -247,7 +255,7 @@ __global__ void __launch_bounds__(P) beam_kernel(BeamArgs a) {
     __syncthreads();
     // new beams (tree_ops.py:35-43)
     float n_sc = 0.f, n_key = 0.f;
-    int n_fl = 0, n_lv = 0, n_pc = 0, n_al = 0, p_ = 0, c_ = 0;
+    int n_fl = 0, n_lv = 0, n_pc = 0, n_ppc = 0, n_al = 0, p_ = 0, c_ = 0;
     if (tid < W) {
       const int id = si[tid];
       n_key = sk[tid];
@@ -257,6 +265,7 @@ __global__ void __launch_bounds__(P) beam_kernel(BeamArgs a) {
       n_fl = c_fl[id];
       n_lv = c_lv[id];
       n_pc = s_cand[p_];
+      n_ppc = s_pc[p_];
       n_al = s_al[p_] && (c_ == 0);
     }
     __syncthreads();
@@ -266,6 +275,7 @@ __global__ void __launch_bounds__(P) beam_kernel(BeamArgs a) {
       s_fl[tid] = n_fl;
       s_lv[tid] = n_lv;
       s_pc[tid] = n_pc;
+      s_ppc[tid] = n_ppc;
       s_al[tid] = n_al;
       s_cand[tid] = c_;
       K[s * W + tid] = n_key;
@@ -438,6 +448,7 @@ int dft_beam_launch(const dft_build_params* p, const float* lp, const int32_t* i
   a.lmax = p->lmax;
   a.chain_first = p->chain_first;
   a.use_ngram = p->use_ngram;
+  a.order = dft::pmi_order_of(p);
   a.lam_a = p->lam_a;
   a.lam_p = p->lam_p;
   a.lp = lp;
@@ -462,6 +473,7 @@ int dft_check_build_params(const dft_build_params* p) {
   if (p->S < 1 || p->S > kMaxS) return DFT_ERR_UNSUPPORTED;
   if (p->B <= 0 || p->B > 65535 || p->V < kM) return DFT_ERR_INVALID;
   if (p->lmax < 1) return DFT_ERR_INVALID;
+  if (p->pmi_order != 0 && (p->pmi_order < 2 || p->pmi_order > 4)) return DFT_ERR_INVALID;
   const int W = p->N - 1 > kM ? p->N - 1 : kM;
   if (W > 64 || (int64_t)p->S * W < p->N - 1) return DFT_ERR_UNSUPPORTED;
   return DFT_OK;

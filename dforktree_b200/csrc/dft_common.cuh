@@ -49,13 +49,22 @@ __device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v
 inline bool valid_dtype(int d) { return d == DFT_F32 || d == DFT_BF16 || d == DFT_F16; }
 
 // Score + build scratch layout (drafter lp / ids / rest rows, then the dense
-// order-3 PMI tensor T), shared by dft_score_build's caller workspace and
+// PMI tensor T of the closure's order), shared by dft_score_build's caller workspace and
 // dft_score_build_static's fixed array, so both use the same offsets.
 struct BuildScratch {
   int64_t lp, ids, rest, T, total;
 };
 
 inline int64_t up256(int64_t x) { return (x + 255) & ~(int64_t)255; }
+
+// n-gram order of the PMI closure (0 selects the Builder's order 3) and the
+// floats of T per (request, step): M^order.
+inline int pmi_order_of(const dft_build_params* p) { return p->pmi_order == 0 ? 3 : p->pmi_order; }
+inline int64_t pmi_step_floats(const dft_build_params* p) {
+  int64_t n = 1;
+  for (int k = 0; k < pmi_order_of(p); ++k) n *= p->M;
+  return n;
+}
 
 inline BuildScratch build_scratch_layout(const dft_build_params* p) {
   BuildScratch w;
@@ -64,7 +73,7 @@ inline BuildScratch build_scratch_layout(const dft_build_params* p) {
   w.lp = o; o = up256(o + rows * p->M * 4);
   w.ids = o; o = up256(o + rows * p->M * 4);
   w.rest = o; o = up256(o + rows * 4);
-  w.T = o; o = up256(o + (p->use_ngram ? (int64_t)p->B * (p->S - 1) * p->M * p->M * p->M * 4 : 0));
+  w.T = o; o = up256(o + (p->use_ngram ? (int64_t)p->B * (p->S - 1) * pmi_step_floats(p) * 4 : 0));
   w.total = o;
   return w;
 }
@@ -167,6 +176,9 @@ __device__ __forceinline__ uint4 ldg_slot(const Slot* s) {
 __device__ __forceinline__ unsigned long long slot_key(uint4 v) {
   return (static_cast<unsigned long long>(v.y) << 32) | v.x;
 }
+// What a probe that misses returns: the empty key (so `slot_key(s) == q` is
+// an exact hit test, also for key 0) with zero counts and rank.
+__device__ __forceinline__ uint4 miss_slot() { return make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0u, 0u); }
 
 // Device view of the n-gram tables (POD, passed by value).  Each slot array
 // has a fingerprint array beside it, one byte per slot: 0 for an empty slot,
@@ -207,7 +219,7 @@ __device__ __forceinline__ uint32_t fp_byte(uint2 w, int k) { return ((k < 4 ? w
 
 // Probe with fingerprints from bucket `idx` on (fingerprint f of key q):
 // fingerprint bytes decide emptiness and candidates; only a candidate's slot
-// is read.  Returns the matching slot or a zero slot.
+// is read.  Returns the matching slot or miss_slot().
 static __device__ __noinline__ uint4 probe_fp_from(const Slot* tab, const uint8_t* fp, unsigned long long mask,
                                             unsigned long long uq, uint32_t f, unsigned long long idx,
                                             int32_t* status) {
@@ -217,7 +229,7 @@ static __device__ __noinline__ uint4 probe_fp_from(const Slot* tab, const uint8_
     for (int k = (int)(idx & 7); k < 8 && n <= mask; ++k, ++n) {
       const uint32_t b = fp_byte(w, k);
       const unsigned long long at = (idx & ~7ull) + k;
-      if (b == 0) return make_uint4(0, 0, 0, 0);
+      if (b == 0) return miss_slot();
       if (b == f) {
         const uint4 s = __ldg(reinterpret_cast<const uint4*>(tab + at));
         if (((static_cast<unsigned long long>(s.y) << 32) | s.x) == uq) return s;
@@ -226,22 +238,22 @@ static __device__ __noinline__ uint4 probe_fp_from(const Slot* tab, const uint8_
     idx = ((idx & ~7ull) + 8) & mask;
   }
   raise_status(status, DFT_DEV_PROBE_LIMIT);
-  return make_uint4(0, 0, 0, 0);
+  return miss_slot();
 }
 
-// Probe an open-addressed table; returns the matching slot (key == q) or a
-// zero slot on a miss.  Negative keys never match (table keys are >= 0).
+// Probe an open-addressed table; returns the matching slot (key == q) or
+// miss_slot() on a miss.  Negative keys never match (table keys are >= 0).
 // With fingerprints (fp != nullptr) the slots are read only on a fingerprint match.
 __device__ __forceinline__ uint4 probe_fp(const Slot* tab, const uint8_t* fp, unsigned long long mask, long long q,
                                           int32_t* status) {
-  if (q < 0 || tab == nullptr) return make_uint4(0, 0, 0, 0);
+  if (q < 0 || tab == nullptr) return miss_slot();
   const unsigned long long uq = static_cast<unsigned long long>(q), h = mix64(uq);
   return probe_fp_from(tab, fp, mask, uq, fp_of(h), h & mask, status);
 }
 
 __device__ __forceinline__ uint4 probe(const Slot* tab, unsigned long long mask, long long q,
                                        int32_t* status) {
-  uint4 z = make_uint4(0, 0, 0, 0);
+  const uint4 z = miss_slot();
   if (q < 0 || tab == nullptr) return z;
   unsigned long long uq = static_cast<unsigned long long>(q);
   unsigned long long h = mix64(uq) & mask;
@@ -259,7 +271,7 @@ __device__ __forceinline__ uint4 probe(const Slot* tab, unsigned long long mask,
 // Continue probing after a first slot `s0` was loaded from bucket mix64(q)&mask.
 __device__ __forceinline__ uint4 probe_from(const Slot* tab, unsigned long long mask, long long q, uint4 s0,
                                             int32_t* status) {
-  uint4 z = make_uint4(0, 0, 0, 0);
+  const uint4 z = miss_slot();
   if (q < 0 || tab == nullptr) return z;
   unsigned long long uq = static_cast<unsigned long long>(q);
   unsigned long long k = slot_key(s0);
@@ -301,6 +313,10 @@ __device__ __forceinline__ float p2_from(float n_bc, float prev_b, float pn_c, f
 // p3 = (n_abc + beta3 * p2) / (n_ab + beta3)               (ngram_gpu.py:44-51)
 __device__ __forceinline__ float p3_from(float n_abc, float n_ab, float p2, float beta3) {
   return __fdiv_rn(__fadd_rn(n_abc, __fmul_rn(beta3, p2)), __fadd_rn(n_ab, beta3));
+}
+// p4 = (c4 + beta4 * p3) / (n4 + beta4)                    (ngram_gpu.py:53-61)
+__device__ __forceinline__ float p4_from(float c4, float n4, float p3, float beta4) {
+  return __fdiv_rn(__fadd_rn(c4, __fmul_rn(beta4, p3)), __fadd_rn(n4, beta4));
 }
 // pmi = clamp(log p - log pn[c], -clip, clip)               (ngram_gpu.py:70)
 __device__ __forceinline__ float pmi_from(float p, float log_pn, float clip) {

@@ -26,7 +26,7 @@ int dft_check_build_params(const dft_build_params* p);
 namespace {
 
 // 32 MiB: 64 requests at S = 24 need 24.3 MB (lp, ids, rest and the dense
-// order-3 PMI tensor T of 23 x 16^3 floats per request).
+// order-3 PMI tensor T of 23 x 16^3 floats per request; order 4 needs 16x that).
 constexpr int64_t kStaticScratchBytes = 32ll << 20;
 constexpr int kMaxDevices = 64;
 
@@ -88,6 +88,7 @@ extern "C" int dft_score_build_static(const dft_table* table, const dft_build_pa
   if (rc) return rc;
   if (!logits || !root || !out) return DFT_ERR_INVALID;
   if (p->use_ngram && !table) return DFT_ERR_INVALID;
+  if (p->use_ngram && dft::pmi_order_of(p) == 4 && !pre1) return DFT_ERR_INVALID;
   if (!dft::valid_dtype(logits_dtype)) return DFT_ERR_INVALID;
   if (ld_s < p->V || ld_b < (int64_t)p->S * ld_s - (ld_s - p->V)) return DFT_ERR_INVALID;
   // the same scratch layout as dft_score_build's workspace

@@ -563,8 +563,7 @@ __device__ float p4_query(const TableView& t, long long z, long long a, long lon
       }
     }
   }
-  float p3 = p3_query(t, a, b, c, st);
-  return __fdiv_rn(__fadd_rn(c4, __fmul_rn(t.beta4, p3)), __fadd_rn(n4, t.beta4));
+  return p4_from(c4, n4, p3_query(t, a, b, c, st), t.beta4);
 }
 
 __global__ void ngram_eval_kernel(TableView t, int order, int what, const int64_t* __restrict__ z,
@@ -596,7 +595,7 @@ __device__ __forceinline__ uint2 fp_round1(const uint8_t* fp, unsigned long long
 
 __device__ __forceinline__ uint4 fp_round2(const Slot* tab, const uint8_t* fp, unsigned long long mask, long long q,
                                            uint2 w, int32_t* st) {
-  const uint4 z = make_uint4(0, 0, 0, 0);
+  const uint4 z = miss_slot();
   if (q < 0 || tab == nullptr) return z;
   const unsigned long long uq = static_cast<unsigned long long>(q), h = mix64(uq), idx = h & mask;
   const uint32_t f = fp_of(h);
@@ -690,6 +689,144 @@ __global__ void __launch_bounds__(256) pmi_dense_kernel(TableView t, int S, cons
   }
 }
 
+// Order 2: T[j, l] = PMI2(b_j, c_l), b = ids[t], c = ids[t+1]
+// (tree_ops.py:59-60); one thread per entry.
+__global__ void __launch_bounds__(256) pmi_dense2_kernel(TableView t, int S, const int32_t* __restrict__ ids,
+                                                         float* __restrict__ T, int32_t* st) {
+  const int tstep = blockIdx.x, req = blockIdx.y, tid = threadIdx.x;
+  const int32_t* idr = ids + (int64_t)req * S * kM;
+  const long long b = idr[tstep * kM + (tid >> 4)], c = idr[(tstep + 1) * kM + (tid & 15)];
+  const uint64_t pol = l2_evict_last_policy();
+  const long long q = b * t.V + c;
+  const uint2 w = fp_round1(t.pair_fp, t.pair_mask, q, pol);
+  const float pnc = pn_at(t, c, st), prevb = prev_at(t, b, st);
+  const uint4 s = fp_round2(t.pair, t.pair_fp, t.pair_mask, q, w, st);
+  const float p2 = p2_from(__uint_as_float(s.z), prevb, pnc, t.beta2);
+  T[((int64_t)req * (S - 1) + tstep) * (kM * kM) + tid] = pmi_from(p2, logf(pnc), t.clip);
+}
+
+// Order 4: T[h, j, k, l] = PMI4(z_h, a_j, b_k, c_l) with z = E[t], a = E[t+1],
+// b = ids[t], c = ids[t+1] and E = [pre1; root; ids] (tree_ops.py:63-64).
+// 512 threads per (request, step) in three phases, each with its shared
+// inputs resolved once:
+//   1. the 256 context pairs (a_j, b_k) and 256 bigrams (b_k, c_l);
+//   2. the 16^3 trigrams (a_j, b_k, c_l) -> p3, and the 16^3 context
+//      trigrams (z_h, a_j, b_k) -> rank i3 in keys3 (-1: absent) and
+//      n4 = n4c[i3] (ngram_gpu.py:57-58);
+//   3. the 16^4 quadgrams (i3, c_l), 16 probes in flight per thread, then
+//      T written coalesced.
+// At t = 0 (z, a constant) and t = 1 (z constant) phase 2 resolves only the
+// distinct rows; phase 3 reads them through the collapsed indices.
+constexpr int kP4Threads = 512;
+struct P4Smem {
+  long long sz[kM], sa[kM], sb[kM], sc[kM];
+  float nab[kM * kM], p2[kM * kM], lpn[kM];
+  float p3[kM * kM * kM];
+  float n4[kM * kM * kM];
+  int i3[kM * kM * kM];
+};
+
+__global__ void __launch_bounds__(kP4Threads) pmi_dense4_kernel(TableView t, int S, const int32_t* __restrict__ ids,
+                                                                const int64_t* __restrict__ root,
+                                                                const int64_t* __restrict__ pre1,
+                                                                float* __restrict__ T, int32_t* st) {
+  extern __shared__ __align__(16) unsigned char p4_raw[];
+  P4Smem& sm = *reinterpret_cast<P4Smem*>(p4_raw);
+  const int tstep = blockIdx.x, req = blockIdx.y, tid = threadIdx.x;
+  const int32_t* idr = ids + (int64_t)req * S * kM;
+  if (tid < kM) {
+    sm.sz[tid] = tstep == 0 ? (long long)pre1[req]
+                            : (tstep == 1 ? (long long)root[req] : (long long)idr[(tstep - 2) * kM + tid]);
+    sm.sa[tid] = tstep == 0 ? (long long)root[req] : (long long)idr[(tstep - 1) * kM + tid];
+    sm.sb[tid] = idr[tstep * kM + tid];
+    sm.sc[tid] = idr[(tstep + 1) * kM + tid];
+  }
+  __syncthreads();
+  const long long V = t.V;
+  const uint64_t pol = l2_evict_last_policy();
+  // distinct rows: a_j varies from t = 1 on, z_h from t = 2 on
+  const int ja = tstep >= 1 ? 16 : 1, hz = tstep >= 2 ? 16 : 1;
+  {  // phase 1: threads 0-255 the context pair (a_j, b_k), 256-511 the bigram (b_k, c_l)
+    const int x = tid & 255, hi = x >> 4, lo = x & 15;
+    long long q;
+    float pnc = 0.f, prevb = 0.f;
+    if (tid < 256) {
+      const long long a = sm.sa[hi], b = sm.sb[lo];
+      q = (a >= 0 && b >= 0 && t.has_ctx) ? a * V + b : -1;
+    } else {
+      const long long b = sm.sb[hi], c = sm.sc[lo];
+      q = b * V + c;
+      pnc = pn_at(t, c, st);
+      prevb = prev_at(t, b, st);
+    }
+    const uint2 w = fp_round1(t.pair_fp, t.pair_mask, q, pol);
+    const uint4 s = fp_round2(t.pair, t.pair_fp, t.pair_mask, q, w, st);
+    if (tid < 256) {
+      sm.nab[x] = __uint_as_float(s.w);
+    } else {
+      sm.p2[x] = p2_from(__uint_as_float(s.z), prevb, pnc, t.beta2);
+      if (hi == 0) sm.lpn[lo] = logf(pnc);
+    }
+  }
+  __syncthreads();
+  {  // phase 2: 8 trigram + 8 context-trigram probes per thread
+    long long q[16];
+    uint2 w[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const int e = tid + kP4Threads * (r & 7);  // 0 .. 4095
+      const int hi = e >> 8, mid = (e >> 4) & 15, lo = e & 15;
+      if (r < 8) {  // (a_hi, b_mid, c_lo)
+        const long long a = sm.sa[hi], b = sm.sb[mid];
+        q[r] = (hi < ja && a >= 0 && b >= 0 && t.has_trip) ? (a * V + b) * V + sm.sc[lo] : -1;
+      } else {      // (z_hi, a_mid, b_lo)
+        const long long z = sm.sz[hi], a = sm.sa[mid], b = sm.sb[lo];
+        q[r] = (hi < hz && mid < ja && z >= 0 && a >= 0 && b >= 0 && t.has_trip) ? (z * V + a) * V + b : -1;
+      }
+      w[r] = fp_round1(t.trip_fp, t.trip_mask, q[r], pol);
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const int e = tid + kP4Threads * (r & 7);
+      const int hi = e >> 8, mid = (e >> 4) & 15, lo = e & 15;
+      const uint4 s = fp_round2(t.trip, t.trip_fp, t.trip_mask, q[r], w[r], st);
+      if (r < 8) {
+        if (hi < ja) sm.p3[e] = p3_from(__uint_as_float(s.z), sm.nab[hi * 16 + mid], sm.p2[mid * 16 + lo], t.beta3);
+      } else if (hi < hz && mid < ja) {
+        const bool hit = q[r] >= 0 && slot_key(s) == static_cast<unsigned long long>(q[r]);
+        const int i3 = hit ? (int)s.w : -1;
+        sm.i3[e] = i3;
+        sm.n4[e] = (hit && t.has_quad) ? __ldg(t.n4c + i3) : 0.f;
+      }
+    }
+  }
+  __syncthreads();
+  float* Tout = T + ((int64_t)req * (S - 1) + tstep) * (kM * kM * kM * kM);
+  const int hmask = hz > 1 ? 15 : 0, jmask = ja > 1 ? 15 : 0;
+  // phase 3: 128 quadgrams per thread in batches of 16
+  for (int r0 = 0; r0 < 128; r0 += 16) {
+    long long q[16];
+    uint2 w[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const int e = tid + kP4Threads * (r0 + r);
+      const int h = (e >> 12) & hmask, j = (e >> 8) & jmask, k = (e >> 4) & 15, l = e & 15;
+      const int i3 = sm.i3[(h * 16 + j) * 16 + k];
+      q[r] = (i3 >= 0 && t.has_quad) ? (long long)i3 * V + sm.sc[l] : -1;
+      w[r] = fp_round1(t.quad_fp, t.quad_mask, q[r], pol);
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const int e = tid + kP4Threads * (r0 + r);
+      const int h = (e >> 12) & hmask, j = (e >> 8) & jmask, k = (e >> 4) & 15, l = e & 15;
+      const uint4 s = fp_round2(t.quad, t.quad_fp, t.quad_mask, q[r], w[r], st);
+      const float p4 = p4_from(__uint_as_float(s.z), sm.n4[(h * 16 + j) * 16 + k], sm.p3[(j * 16 + k) * 16 + l],
+                               t.beta4);
+      Tout[e] = pmi_from(p4, sm.lpn[l], t.clip);
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" int dft_ngram_eval(const dft_table* table, int order, int what, const int64_t* z, const int64_t* a,
@@ -708,9 +845,20 @@ extern "C" int dft_ngram_eval(const dft_table* table, int order, int what, const
 
 int dft_pmi_dense_launch(const dft_table* table, const dft_build_params* p, const int32_t* ids, const int64_t* root,
                          const int64_t* pre1, float* T, int32_t* dev_status, cudaStream_t st) {
-  (void)pre1;  // order 3 does not read pre1 (E[0] is used by order 4 only)
   dim3 grid(p->S - 1, p->B);
-  pmi_dense_kernel<<<grid, 256, 0, st>>>(table->view, p->S, ids, root, pre1, T, dev_status);
+  const int order = dft::pmi_order_of(p);
+  if (order == 2) {
+    pmi_dense2_kernel<<<grid, 256, 0, st>>>(table->view, p->S, ids, T, dev_status);
+  } else if (order == 3) {
+    pmi_dense_kernel<<<grid, 256, 0, st>>>(table->view, p->S, ids, root, pre1, T, dev_status);
+  } else {
+    if (!pre1) return DFT_ERR_INVALID;   // E[0] = pre1 is order 4's first context token
+    static_assert(sizeof(P4Smem) <= 227 * 1024, "order-4 PMI shared memory");
+    if (cudaFuncSetAttribute(pmi_dense4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(P4Smem)) !=
+        cudaSuccess)
+      return DFT_ERR_CUDA;
+    pmi_dense4_kernel<<<grid, kP4Threads, sizeof(P4Smem), st>>>(table->view, p->S, ids, root, pre1, T, dev_status);
+  }
   DFT_LAUNCH_CHECK();
   return DFT_OK;
 }
@@ -720,5 +868,7 @@ extern "C" int dft_pmi_dense(const dft_table* table, const dft_build_params* p, 
   if (!table || !p || !ids || !root || !T) return DFT_ERR_INVALID;
   if (p->M != kM) return DFT_ERR_UNSUPPORTED;
   if (p->B <= 0 || p->S < 2 || p->B > 65535) return DFT_ERR_INVALID;
+  if (p->pmi_order != 0 && (p->pmi_order < 2 || p->pmi_order > 4)) return DFT_ERR_INVALID;
+  if (dft::pmi_order_of(p) == 4 && !pre1) return DFT_ERR_INVALID;
   return dft_pmi_dense_launch(table, p, ids, root, pre1, T, dev_status, reinterpret_cast<cudaStream_t>(stream));
 }

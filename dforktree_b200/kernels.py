@@ -114,9 +114,16 @@ def ngram_eval(table: Table, order: int, what: int, z, a, b, c, status=None) -> 
 
 
 # ---------------------------------------------------------- score + build --
-def build_params(B, S, V, N, M=16, lmax=99, chain_first=False, use_ngram=True, lam_a=0.3, lam_p=0.6):
+def build_params(B, S, V, N, M=16, lmax=99, chain_first=False, use_ngram=True, lam_a=0.3, lam_p=0.6, order=3):
     return L.BuildParams(B=B, S=S, V=V, M=M, N=N, lmax=lmax, chain_first=int(bool(chain_first)),
-                         use_ngram=int(bool(use_ngram)), lam_a=lam_a, lam_p=lam_p)
+                         use_ngram=int(bool(use_ngram)), lam_a=lam_a, lam_p=lam_p, pmi_order=order)
+
+
+def pmi_step_shape(order: int, M: int = 16):
+    """Shape of T per (request, step) for the closure's n-gram order."""
+    if order not in (2, 3, 4):
+        raise ValueError(f"n-gram order must be 2, 3 or 4, not {order}")
+    return (M,) * order
 
 
 def _logits_view(logits: torch.Tensor):
@@ -141,15 +148,21 @@ def score(logits: torch.Tensor, M: int = 16):
     return lp, ids, rest
 
 
-def pmi_dense(table: Table, ids: torch.Tensor, root: torch.Tensor, pre1: torch.Tensor = None, status=None):
-    """Dense PMI T [B, S-1, M, M, M] over E = [pre1; root; ids] (tree_ops.py:56-65)."""
+def pmi_dense(table: Table, ids: torch.Tensor, root: torch.Tensor, pre1: torch.Tensor = None, status=None,
+              order: int = 3):
+    """Dense PMI T over E = [pre1; root; ids] (tree_ops.py:56-65): [B, S-1, M, M]
+    for order 2, [B, S-1, M, M, M] for order 3, [B, S-1, M, M, M, M] for
+    order 4 (which reads pre1 as E[0] and requires it)."""
     lib = L.lib()
     B, S, M = ids.shape
+    step = pmi_step_shape(order, M)
+    if order == 4 and pre1 is None:
+        raise L.DFTError("order-4 PMI needs pre1 (E[0])")
     ids = ids.to(torch.int32).contiguous()
     root = root.reshape(B).to(torch.int64).contiguous()
     pre1 = None if pre1 is None else pre1.reshape(B).to(torch.int64).contiguous()
-    p = build_params(B, S, table.V, N=32, M=M)
-    T = torch.empty(B, S - 1, M, M, M, dtype=torch.float32, device=ids.device)
+    p = build_params(B, S, table.V, N=32, M=M, order=order)
+    T = torch.empty(B, S - 1, *step, dtype=torch.float32, device=ids.device)
     L.check(lib.dft_pmi_dense(table.handle, C.byref(p), ids.data_ptr(), root.data_ptr(), L.ptr(pre1),
                               T.data_ptr(), _status_ptr(status), L.stream_handle()), "dft_pmi_dense")
     return T
@@ -179,10 +192,17 @@ def _tree_struct_out(o: dict) -> L.TreeOut:
 
 def beam_build(lp, ids, rest, root, N, T=None, logc=None, c0=None, lmax=99, chain_first=False, lam_a=0.3,
                lam_p=0.6, out=None, status=None, V=None):
+    """The n-gram order of the closure follows from T's rank: T [B, S-1]
+    + (M,) * order."""
     lib = L.lib()
     B, S, M = lp.shape
     use_ngram = T is not None
-    p = build_params(B, S, V or 1 << 20, N, M, lmax, chain_first, use_ngram, lam_a, lam_p)
+    order = 3
+    if use_ngram:
+        order = T.dim() - 2
+        if T.shape != (B, S - 1, *pmi_step_shape(order, M)) or not T.is_contiguous():
+            raise L.DFTError(f"T must be a contiguous [B, S-1] + (M,) * order tensor, got {tuple(T.shape)}")
+    p = build_params(B, S, V or 1 << 20, N, M, lmax, chain_first, use_ngram, lam_a, lam_p, order)
     out = tree_outputs(B, S, N, lp.device) if out is None else out
     to = _tree_struct_out(out)
     L.check(lib.dft_beam_build(C.byref(p), lp.contiguous().data_ptr(), ids.to(torch.int32).contiguous().data_ptr(),
@@ -192,8 +212,8 @@ def beam_build(lp, ids, rest, root, N, T=None, logc=None, c0=None, lmax=99, chai
     return out
 
 
-def score_build_workspace(B, S, V, N, use_ngram=True, M=16, device=None) -> torch.Tensor:
-    p = build_params(B, S, V, N, M, use_ngram=use_ngram)
+def score_build_workspace(B, S, V, N, use_ngram=True, M=16, device=None, order=3) -> torch.Tensor:
+    p = build_params(B, S, V, N, M, use_ngram=use_ngram, order=order)
     nbytes = L.load().dft_score_build_workspace_bytes(C.byref(p))
     if nbytes < 0:
         raise L.DFTError("unsupported score_build shape")
@@ -201,11 +221,13 @@ def score_build_workspace(B, S, V, N, use_ngram=True, M=16, device=None) -> torc
 
 
 def score_build(table, logits, root, pre1, N, workspace, out, lmax=99, chain_first=False, use_ngram=True,
-                lam_a=0.3, lam_p=0.6, status=None):
-    """Builder.run (fc1_builder.py:26-47) for a batch: three launches."""
+                lam_a=0.3, lam_p=0.6, status=None, order=3):
+    """Builder.run (fc1_builder.py:26-47) for a batch: three launches.  `order`
+    is the n-gram order of the closure (the Builder's is 3); the workspace
+    must be sized for the same order."""
     lib = L.lib()
     x, B, S, V, sb, ss = _logits_view(logits)
-    p = build_params(B, S, V, N, 16, lmax, chain_first, use_ngram, lam_a, lam_p)
+    p = build_params(B, S, V, N, 16, lmax, chain_first, use_ngram, lam_a, lam_p, order)
     to = _tree_struct_out(out)
     L.check(lib.dft_score_build(None if table is None else table.handle, C.byref(p), x.data_ptr(), L.dtype_code(x),
                                 sb, ss, root.data_ptr(), L.ptr(pre1), workspace.data_ptr(), C.byref(to),
@@ -214,12 +236,12 @@ def score_build(table, logits, root, pre1, N, workspace, out, lmax=99, chain_fir
 
 
 def score_build_static(table, logits, root, pre1, N, out, lmax=99, chain_first=False, use_ngram=True, lam_a=0.3,
-                       lam_p=0.6, status=None):
+                       lam_p=0.6, status=None, order=3):
     """score_build without a workspace: the library's fixed-size device
     scratch (dft_score_build_static); for callers that cannot allocate."""
     lib = L.lib()
     x, B, S, V, sb, ss = _logits_view(logits)
-    p = build_params(B, S, V, N, 16, lmax, chain_first, use_ngram, lam_a, lam_p)
+    p = build_params(B, S, V, N, 16, lmax, chain_first, use_ngram, lam_a, lam_p, order)
     to = _tree_struct_out(out)
     L.check(lib.dft_score_build_static(None if table is None else table.handle, C.byref(p), x.data_ptr(),
                                        L.dtype_code(x), sb, ss, root.data_ptr(), L.ptr(pre1), C.byref(to),

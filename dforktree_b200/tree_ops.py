@@ -17,30 +17,37 @@ from . import kernels as K
 @dataclass
 class PathFn:
     """The fork-aware scoring closure of `ngram_path_fn` (tree_ops.py:55-66),
-    as data: the dense PMI tensor T [B, S-1, M, M, M], drafter lp [B, S, M],
-    out-of-list mass rest [B, S], ids [B, S, M] and the two weights.  The
-    reference ships the function without its closure; the device kernel
-    evaluates  lc = x - logsumexp([x, rest[s]]),
-    x = lp[s] + (lam_a if on-top-1-path else lam_p) * T[s-1, pc, cand]."""
+    as data: the dense PMI tensor T [B, S-1] + (M,) * order, drafter lp
+    [B, S, M], out-of-list mass rest [B, S], ids [B, S, M] and the two
+    weights.  The reference ships the function without its closure; the
+    device kernel evaluates  lc = x - logsumexp([x, rest[s]]),
+    x = lp[s] + (lam_a if on-top-1-path else lam_p) * t  with the closure
+    arguments cand, pc, ppc (the beam's candidates at positions s-1, s-2,
+    s-3) indexing T by order: t = T[s-1, cand] (2), T[s-1, pc, cand] (3),
+    T[s-1, ppc, pc, cand] (4)."""
     T: torch.Tensor
     lp: torch.Tensor
     rest: torch.Tensor
     ids: torch.Tensor
     lam_a: float
     lam_p: float
+    order: int = 3
 
 
 def ngram_path_fn(ng, order, ids, lp, rest, pre1, root, lam_a, lam_p) -> PathFn:
-    """tree_ops.py:55-66 (order 3): builds T on the device."""
-    if order != 3:
-        raise NotImplementedError("the device closure implements the order-3 path the Builder uses")
+    """tree_ops.py:55-66: builds T for n-gram order 2, 3 or 4 on the device
+    (order 4 reads pre1 as E[0]; the reference's torch.cat needs it for every
+    order, the device kernels of orders 2 and 3 never read it)."""
+    if order not in (2, 3, 4):
+        raise ValueError(f"n-gram order must be 2, 3 or 4, not {order}")
     b3 = ids.dim() == 2
     ids_b = ids.unsqueeze(0) if b3 else ids
     lp_b = lp.unsqueeze(0) if b3 else lp
     rest_b = rest.unsqueeze(0) if b3 else rest
     B = ids_b.shape[0]
-    T = K.pmi_dense(ng.table, ids_b, root.reshape(B), None if pre1 is None else pre1.reshape(B), ng.status)
-    return PathFn(T, lp_b.float().contiguous(), rest_b.float().contiguous(), ids_b, lam_a, lam_p)
+    T = K.pmi_dense(ng.table, ids_b, root.reshape(B), None if pre1 is None else pre1.reshape(B), ng.status,
+                    order=order)
+    return PathFn(T, lp_b.float().contiguous(), rest_b.float().contiguous(), ids_b, lam_a, lam_p, order)
 
 
 def beam_tree(c0, logc, N, lmax, chain_first=True, path_fn: PathFn = None, S=None, root=None):

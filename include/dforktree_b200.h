@@ -115,6 +115,9 @@ typedef struct {
   int32_t chain_first;  /* FC1_CHAIN_FIRST (BIG = 1e4 bonus, tree_ops.py:13) */
   int32_t use_ngram;    /* 1: fork-aware PMI closure; 0: plain renormalised  */
   float lam_a, lam_p;   /* 0.3, 0.6 (fc1_builder.py:31)                      */
+  int32_t pmi_order;    /* n-gram order of the closure: 2, 3 or 4 (the second
+                           argument of ngram_path_fn, tree_ops.py:55); 0 = 3,
+                           the Builder's (fc1_builder.py:31)                  */
 } dft_build_params;
 
 typedef struct {
@@ -138,8 +141,12 @@ typedef struct {
 DFT_API int dft_score(const dft_build_params* p, const void* logits, int32_t logits_dtype, int64_t ld_b, int64_t ld_s,
               float* lp, int32_t* ids, float* rest, void* stream);
 
-/* Dense PMI tensor T[b, t, i, j, l] of ngram_path_fn (tree_ops.py:56-65),
- * order 3, over E = [pre1; root; ids].  T is [B, S-1, M, M, M] float.       */
+/* Dense PMI tensor T of ngram_path_fn (tree_ops.py:56-65) over
+ * E = [pre1; root; ids], for p->pmi_order (0 = 3):
+ *   order 2: T[b, t, j, l]       = PMI2(E[t+2]_j, E[t+3]_l)      [B, S-1, M, M]
+ *   order 3: T[b, t, i, j, l]    = PMI3(E[t+1]_i, .., E[t+3]_l)  [B, S-1, M, M, M]
+ *   order 4: T[b, t, h, i, j, l] = PMI4(E[t]_h, .., E[t+3]_l)    [B, S-1, M, M, M, M]
+ * float.  pre1 is read by order 4 only (NULL there: DFT_ERR_INVALID).       */
 DFT_API int dft_pmi_dense(const dft_table* table, const dft_build_params* p, const int32_t* ids, const int64_t* root,
                   const int64_t* pre1, float* T, int32_t* dev_status, void* stream);
 

@@ -23,7 +23,11 @@ the drafter's top-1"):
 i.e. PMI evidence from the branch's last two tokens with the larger weight
 (lam_p) after the branch leaves the top-1 path, renormalised together with the
 out-of-list mass `rest[s]` exactly like the no-n-gram branch of Builder.run
-(fc1_builder.py:35-36).
+(fc1_builder.py:35-36).  For the other orders `ngram_path_fn` accepts
+(tree_ops.py:59-64) the same closure reads the context its T spans:
+T[s-1, cand[w], l] for order 2 and T[s-1, ppc[w], pc[w], cand[w], l] for
+order 4, `ppc` being the great-grandparent candidate beam_tree carries for it
+(tree_ops.py:24, 40).
 """
 from __future__ import annotations
 
@@ -96,11 +100,16 @@ def dense_pmi(ng, order: int, ids: np.ndarray, pre1: int, root: int) -> np.ndarr
 
 def path_scores(T: np.ndarray, lp: np.ndarray, rest: np.ndarray, lam_a: float, lam_p: float):
     """Reconstructed fork-aware closure fn(s, cand, pc, ppc, al) -> lc [W, M]
-    (PARITY-UNPINNED, see module docstring)."""
+    (PARITY-UNPINNED, see module docstring).  The order follows from T
+    [S-1] + (M,) * order: cand, pc, ppc are the beam's candidates at
+    positions s-1, s-2, s-3, i.e. the order-4 context, so order 2 reads
+    T[s-1][cand], order 3 T[s-1][pc, cand], order 4 T[s-1][ppc, pc, cand]."""
     la, lpn = F32(lam_a), F32(lam_p)
+    order = T.ndim - 1
 
     def fn(s, cand, pc, ppc, al):
-        t = T[s - 1][pc, cand]                                  # [W, M]
+        Ts = T[s - 1]
+        t = Ts[cand] if order == 2 else (Ts[pc, cand] if order == 3 else Ts[ppc, pc, cand])   # [W, M]
         lam = np.where(al, la, lpn).astype(np.float32)[:, None]
         x = (lp[s][None, :] + (lam * t).astype(np.float32)).astype(np.float32)
         r = np.broadcast_to(rest[s], (x.shape[0], 1)).astype(np.float32)

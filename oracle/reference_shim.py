@@ -37,13 +37,17 @@ def load_reference(ref_dir: str, kernels: bool = True):
 
 
 def reconstructed_fn(T, lp, rest, lam_a, lam_p):
-    """Fork-aware closure: x = lp[s] + lam * T[s-1][pc, cand] with lam = lam_a
-    while every ancestor was candidate 0, else lam_p; normalised against the
-    retained out-of-list mass rest[s] (oracle/builder.py `path_scores`)."""
+    """Fork-aware closure: x = lp[s] + lam * t with lam = lam_a while every
+    ancestor was candidate 0, else lam_p; normalised against the retained
+    out-of-list mass rest[s] (oracle/builder.py `path_scores`).  t reads T by
+    its order (T is [S-1] + (M,) * order): T[s-1][cand] for order 2,
+    T[s-1][pc, cand] for 3, T[s-1][ppc, pc, cand] for 4."""
     import torch
+    order = T.dim() - 1
 
     def fn(s, cand, pc, ppc, al):
-        t = T[s - 1][pc, cand]
+        Ts = T[s - 1]
+        t = Ts[cand] if order == 2 else (Ts[pc, cand] if order == 3 else Ts[ppc, pc, cand])
         lam = torch.where(al, lam_a, lam_p)[:, None].to(t.dtype)
         x = lp[s][None, :] + lam * t
         r = rest[s].reshape(1, 1).expand(x.shape[0], 1)

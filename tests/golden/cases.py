@@ -45,6 +45,39 @@ BUILDER_CASES = [
     dict(name="b_v2048_s24_n32_nongram", V=2048, S=24, N=32, nb=60000, nt=200000, chain_first=False, ngram=False, seed=106),
 ]
 
+# The closure at n-gram orders 2 and 4 (tree_ops.ngram_path_fn's `order`,
+# tree_ops.py:59-64; the Builder itself uses 3).  Order-4 tables carry
+# quadgram rows; small V keeps the trees' contexts inside the tables.
+ORDER_CASES = [
+    dict(name="o2_v1024_s16_n32", order=2, V=1024, S=16, N=32, nb=40000, nt=150000, nq=0, chain_first=False,
+         seed=200),
+    dict(name="o4_v256_s10_n32", order=4, V=256, S=10, N=32, nb=20000, nt=120000, nq=400000, chain_first=False,
+         seed=201),
+    dict(name="o4_v512_s8_n64_chain", order=4, V=512, S=8, N=64, nb=30000, nt=150000, nq=300000, chain_first=True,
+         seed=202),
+]
+ORDER_T_SAMPLE = 20000    # T entries kept per fixture (a seeded sample of the full tensor)
+
+
+def order_inputs(case: dict):
+    rng = np.random.default_rng(case["seed"])
+    V, S = case["V"], case["S"]
+    table = synth.make_ngram_table(V, case["nb"], case["nt"], seed=case["seed"] + 7, n_quad=case["nq"])
+    logits = synth.make_logits(S, V, seed=case["seed"] + 13)
+    hot = synth.zipf_ids(rng, S * 8, V).reshape(S, 8)
+    logits[np.arange(S)[:, None], hot] += np.float32(9.0)
+    root = int(synth.zipf_ids(rng, 1, V)[0])
+    pre1 = int(synth.zipf_ids(rng, 1, V)[0])
+    return table, logits, root, pre1
+
+
+def order_t_sample(shape, seed: int = 5):
+    """Flat indices of the T entries a fixture keeps (sorted, distinct)."""
+    n = int(np.prod(shape))
+    k = min(ORDER_T_SAMPLE, n)
+    return np.sort(np.random.default_rng(seed).choice(n, k, replace=False))
+
+
 # Full config-0 vocabulary (V = 248,320, 2M bigram + 8M trigram keys).
 CONFIG0 = dict(V=248320, nb=2_000_000, nt=8_000_000, table_seed=0, S=24, N=32)
 CONFIG0_SEEDS = [0, 1]

@@ -124,6 +124,42 @@ def gen_builder(mods, captured, out_dir, with_config0=True):
             print("config0", seed, out["tokens"][:8], out["parent"][:8])
 
 
+def gen_orders(mods, captured, out_dir):
+    """tree_ops.ngram_path_fn at n-gram orders 2 and 4 and the reference's
+    beam_tree / tree_struct over it: the steps of Builder.run
+    (fc1_builder.py:27-40) with the order argument changed.  Keeps a seeded
+    sample of T (cases.order_t_sample) and the whole tree."""
+    import torch
+    TO = mods["tree_ops"]
+    NG = mods["ngram_gpu"].NGramGPU
+    for case in cases.ORDER_CASES:
+        table, logits, root, pre1 = cases.order_inputs(case)
+        path = _table_file(table)
+        try:
+            ng = NG(path, "cpu", beta3=60.0)
+        finally:
+            os.unlink(path)
+        S, N = case["S"], case["N"]
+        lp, ids = torch.log_softmax(torch.from_numpy(logits).float(), -1).topk(16, -1)
+        rest = torch.log((1 - lp.exp().sum(-1)).clamp(1e-06, 1.0))
+        c0 = lp[0] - torch.logsumexp(torch.cat((lp[0], rest[:1])), 0)
+        captured.clear()
+        fn = TO.ngram_path_fn(ng, case["order"], ids, lp, rest, torch.tensor([pre1]), torch.tensor([root]), 0.3, 0.6)
+        ss, cand, parent, flags = TO.beam_tree(c0, None, N, 99, case["chain_first"], fn, S=S)
+        parent_full = torch.cat((torch.tensor([-1]), parent + 1))
+        anc, depth, cidx = TO.tree_struct(parent_full, 4)
+        T = captured["T"].numpy()
+        sel = cases.order_t_sample(T.shape)
+        out = dict(ids=ids.numpy(), lp=lp.numpy(), T_index=sel, T_sample=T.reshape(-1)[sel],
+                   T_shape=np.asarray(T.shape), ss=ss.numpy(), cand=cand.numpy(), flags=flags.numpy(),
+                   parent=parent_full.numpy(), depth=depth.numpy(), anc=anc.numpy(), cidx=cidx.numpy(),
+                   tokens=torch.cat((torch.tensor([root]), ids[ss, cand])).numpy(),
+                   checksum=cases.checksum(logits, table["keys"], table["keys3"], table.get("keys4", np.zeros(0)),
+                                           [root, pre1]))
+        np.savez_compressed(os.path.join(out_dir, case["name"] + ".npz"), **out)
+        print(case["name"], T.shape, out["tokens"][:8], out["parent"][:8])
+
+
 def gen_gdn(mods, out_dir):
     import torch
     TK = mods["tree_kernels"]
@@ -229,11 +265,13 @@ def main():
         ap.error("give the reference's dforktree/ directory with --ref or DFORKTREE_REF")
     mods = _load_reference(args.ref)
     captured = _patch_path_fn(mods)
-    only = set(args.only.split(",")) if args.only else {"ngram", "builder", "gdn", "conv", "commit"}
+    only = set(args.only.split(",")) if args.only else {"ngram", "builder", "orders", "gdn", "conv", "commit"}
     if "ngram" in only:
         gen_ngram(mods, args.out)
     if "builder" in only:
         gen_builder(mods, captured, args.out, with_config0=not args.no_config0)
+    if "orders" in only:
+        gen_orders(mods, captured, args.out)
     if "gdn" in only:
         gen_gdn(mods, args.out)
     if "conv" in only:

@@ -51,11 +51,24 @@ def test_invalid_arguments_are_rejected_on_the_host(lib):
     assert lib.dft_score_build_workspace_bytes(ctypes.byref(p)) == -1      # N <= 64
     p.N = 32
     assert lib.dft_score_build_workspace_bytes(ctypes.byref(p)) >= 23 * 4096 * 4
+    # the closure's n-gram order: 0 (= 3), 2, 3, 4; T grows by M per order
+    ws = {}
+    for order in (0, 2, 3, 4):
+        p.pmi_order = order
+        ws[order] = lib.dft_score_build_workspace_bytes(ctypes.byref(p))
+    T3 = 23 * 16 ** 3 * 4
+    assert ws[0] == ws[3] and ws[4] - ws[3] >= 15 * T3 - 256 and ws[3] - ws[2] >= 15 * T3 // 16 - 256
+    p.pmi_order = 5
+    assert lib.dft_score_build_workspace_bytes(ctypes.byref(p)) == -1
+    fake = 1 << 20
+    assert lib.dft_pmi_dense(fake, ctypes.byref(p), fake, fake, None, fake, None, None) == 1   # order 5
+    p.pmi_order = 4
+    assert lib.dft_pmi_dense(fake, ctypes.byref(p), fake, fake, None, fake, None, None) == 1   # order 4 needs pre1
+    p.pmi_order = 0
     assert lib.dft_gdn_tree_verify(None, None, None) == 1
     assert lib.dft_gdn_commit(None, None, None) == 1
     # in-place commit (zero end stride) with two end nodes would race on one tile:
     # rejected from the arguments alone (the pointers are never dereferenced)
-    fake = 1 << 20
     ca = L.CommitArgs(L=1, B=1, N=32, Hk=16, Hv=32, Dk=128, Dv=128, P=24, E=2, state_in=fake, state_out=fake,
                       so_su=0, aux_k=fake, aux_vn=fake, aux_g=fake, anc=fake, path=fake, ends=fake)
     assert lib.dft_gdn_commit(ctypes.byref(ca), None, None) == 1
@@ -87,7 +100,7 @@ int main(void) {
   printf("dft_tree_attn_args SIZE %zu\n", sizeof(dft_tree_attn_args));
   F(dft_tree_attn_args, q) F(dft_tree_attn_args, n_slots) F(dft_tree_attn_args, sm_scale)
   F(dft_tree_attn_args, max_kv_len) F(dft_tree_attn_args, o) F(dft_tree_attn_args, o_sh)
-  F(dft_table_desc, max_load) F(dft_table_desc, n4c) F(dft_build_params, lam_p)
+  F(dft_table_desc, max_load) F(dft_table_desc, n4c) F(dft_build_params, lam_p) F(dft_build_params, pmi_order)
   F(dft_conv_args, iw_slots) F(dft_conv_args, y_dtype) F(dft_gdn_args, ag_sh) F(dft_gdn_args, pool)
   F(dft_gdn_args, aux_k_per_v) F(dft_gdn_args, overlap_prev) F(dft_commit_args, ends) F(dft_commit_args, aux_k_per_v) F(dft_commit_args, so_sk)
   return 0;

@@ -50,6 +50,25 @@ def test_builder_oracle_matches_reference(case):
         np.testing.assert_allclose(out["T"], g["T"], rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("case", cases.ORDER_CASES, ids=lambda c: c["name"])
+def test_builder_oracle_other_orders_match_reference(case):
+    """ngram_path_fn at orders 2 and 4 (tree_ops.py:59-64) and the beam over
+    it: T (a seeded sample of its entries) and the whole tree."""
+    g = _load(case["name"])
+    table, logits, root, pre1 = cases.order_inputs(case)
+    np.testing.assert_allclose(g["checksum"], cases.checksum(logits, table["keys"], table["keys3"],
+                                                             table.get("keys4", np.zeros(0)), [root, pre1]))
+    ng = ngram.NGramOracle(table, beta3=60.0)
+    out = builder.builder_run(logits, root, pre1, ng, N=case["N"], chain_first=case["chain_first"],
+                              order=case["order"])
+    assert out["T"].shape == tuple(g["T_shape"]) == (case["S"] - 1,) + (16,) * case["order"]
+    np.testing.assert_array_equal(g["T_index"], cases.order_t_sample(out["T"].shape))
+    np.testing.assert_allclose(out["T"].reshape(-1)[g["T_index"]], g["T_sample"], rtol=1e-5, atol=1e-5)
+    for key in ("tokens", "parent", "depth", "anc", "cidx", "ids", "ss", "cand"):
+        np.testing.assert_array_equal(out[key], g[key], err_msg=key)
+    np.testing.assert_array_equal(out["flags"], g["flags"])
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("seed", cases.CONFIG0_SEEDS)
 def test_builder_oracle_config0_full_vocab(seed):
