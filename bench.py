@@ -47,6 +47,8 @@ C_CONV = 2 * HK * D + HV * D
 VERIFY_BYTES = 2 * 1024 * 1024 + 262144 + 262144 + 8192 + 262144      # S0 + q,k + v + g,beta + o
 # the fused launch also reads the conv state / weights and writes the aux rows the commit needs
 VERIFY_AUX_BYTES = 8192 * 3 * 2 + 262144 + 524288 + 4096               # conv state + k_hat + vn + G
+# the plugin's default tree of 64 nodes (fc1_fused.py:4): q / k / v, gates and o double
+VERIFY_BYTES_N64 = 2 * 1024 * 1024 + 2 * (262144 + 262144 + 8192 + 262144)
 COMMIT_BYTES_FIXED = 4 * 1024 * 1024                                   # read S0 + write S
 COMMIT_BYTES_PER_NODE = 32 * 1024                                      # k, vn rows of 32 heads
 SCORE_BYTES = S * V * 4 + 105984 * 12 + 2944                           # logits + table probes + prev/pn
@@ -466,6 +468,8 @@ def run_ours(args, rank, world, local_rank):
     # ---- tree-masked attention verify of one gated full-attention layer (outside the cycle)
     attn = _bench_attention(args, dev, cyc, g, stream) if args.attn else None
     status = int(cyc.status.item())
+    # ---- the plugin's default 64-node tree (outside the cycle)
+    n64 = _bench_verify_n64(args, dev, table, stream) if args.n64 else None
 
     if rank != 0:
         return None
@@ -505,6 +509,11 @@ def run_ours(args, rank, world, local_rank):
         per_kernel["tree_attn_GBps"] = Bt * ATTN_BYTES / (attn / 1e3) / 1e9
         per_kernel["tree_attn_hbm_frac"] = per_kernel["tree_attn_GBps"] / hbm
         per_kernel["tree_attn_TFLOPs"] = Bt * ATTN_FLOPS / (attn / 1e3) / 1e12
+    if n64 is not None:
+        per_kernel["verify_n64_ms_per_layer"] = n64[0]
+        per_kernel["verify_n64_GBps"] = Bt * VERIFY_BYTES_N64 / (n64[0] / 1e3) / 1e9
+        per_kernel["verify_n64_hbm_frac"] = per_kernel["verify_n64_GBps"] / hbm
+        per_kernel["verify_n64_mean_max_depth"] = n64[1]
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "cycles/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
@@ -635,6 +644,41 @@ def _bench_attention(args, dev, cyc, g, stream):
     if w.device_status():
         raise RuntimeError(f"tree attention raised device status {w.device_status()}")
     return sum(e1.elapsed_time(e2) for e1, e2 in pairs) / len(pairs)
+
+
+def _bench_verify_n64(args, dev, table, stream):
+    """Tree conv + GDN verify of one layer at the plugin's default tree size,
+    64 nodes (fc1_fused.py:4, FC1_TREE_N), on the bench's batch and layer
+    shape: the CUDA-core verifier (the tensor-core one takes up to 32 nodes)
+    behind a separate tree-conv launch.  Mean CUDA-event time per layer over
+    two alternating layers (states 128 MiB per layer: no L2 reuse)."""
+    import torch
+    from dforktree_b200 import workload as WL
+    from dforktree_b200.cycle import CycleConfig, DraftTreeCycle
+    cfg = CycleConfig(B=args.batch, layers=2, N=64)
+    cyc = DraftTreeCycle(cfg, table, dev, seed=7)
+    inp = WL.cycle_inputs(cfg, dev, seed=99)
+    cyc.build(inp["logits"], inp["root"], inp["pre1"])
+    for _ in range(max(args.warmup, 3)):
+        for l in range(2):
+            cyc.verify_layer(l, inp["x"][l], inp["a"][l], inp["b"][l])
+    mk = lambda: torch.cuda.Event(enable_timing=True)
+    pairs = []
+    for _ in range(max(args.steps, 5)):
+        for l in range(2):
+            e1, e2 = mk(), mk()
+            e1.record(stream)
+            cyc.verify_layer(l, inp["x"][l], inp["a"][l], inp["b"][l])
+            e2.record(stream)
+            pairs.append((e1, e2))
+    torch.cuda.synchronize()
+    if int(cyc.status.item()):
+        raise RuntimeError(f"N=64 verify raised device status {int(cyc.status.item())}")
+    depth = float(cyc.tree["depth"].max(1).values.float().mean())
+    ms = sum(e1.elapsed_time(e2) for e1, e2 in pairs) / len(pairs)
+    del cyc, inp
+    torch.cuda.empty_cache()
+    return ms, depth
 
 
 def run_profile_attention(args):
@@ -844,6 +888,8 @@ def main():
                     help="config-4 stage: requests split over the GPUs (0 skips the stage)")
     ap.add_argument("--no-attn", dest="attn", action="store_false",
                     help="skip the tree-masked attention stage (reported under stages, outside the cycle)")
+    ap.add_argument("--no-n64", dest="n64", action="store_false",
+                    help="skip the 64-node verify stage (reported under stages, outside the cycle)")
     ap.add_argument("--profile", action="store_true", help="only W + K plain cycles (for ncu); prints nothing")
     ap.add_argument("--profile-attn", action="store_true",
                     help="only W + K tree-attention layers at the bench shape (for ncu); prints nothing")
