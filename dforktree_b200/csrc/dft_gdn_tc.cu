@@ -615,11 +615,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // head hh's A / PD / A' are written: release its two solver warps
-      // (named barrier 2 + hh: the four C1 warps of the head arrive, the two
-      // solver warps wait; no other warp waits for C1)
-      asm volatile("bar.arrive %0, %1;" ::"r"(2 + hh), "r"(192) : "memory");
+      // (named barrier 2 + hh: the C1 warps of the head arrive, the two solver
+      // warps wait; no other warp waits for C1).  Head 1's solvers are its C1
+      // warps 4 and 5 themselves: they wait rather than arrive
+      if (!(R == 2 && (warp == 4 || warp == 5)))
+        asm volatile("bar.arrive %0, %1;" ::"r"(2 + hh), "r"(hh ? 128 : 192) : "memory");
     }
-    // ------------------------------------------------ X, Z per head (warps 2, 3 / 6, 7)
+    // ------------------------------------------------ X, Z per head (warps 2, 3 / 4, 5)
     // Both are unit lower-triangular solves r_i = init_i - sum_{m < i} L[i][m] r_m,
     // one column / row per lane, in registers:
     //   X = (I + A)^-1:  L = A,  init = e_c (lane c = column c of X)
@@ -627,10 +629,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     //   init = row n of PD reversed, z_j = r_{31-j} (lane n = row n of Z)
     // They go into the [X; Z] operand (hi / lo tf32 split) over [k; q] once
     // every M1 has retired.
-    if ((warp & 3) >= 2 && (warp >> 2) < R) {
-      const int hh = warp >> 2;
+    // The four solver warps sit on the four SM sub-partitions (warp % 4):
+    // head 0's on warps 2, 3, head 1's on warps 4, 5 once their C1 part is done.
+    if (warp == 2 || warp == 3 || (R == 2 && (warp == 4 || warp == 5))) {
+      const int hh = warp >= 4 ? 1 : 0;
       const bool zw = warp & 1;
-      named_bar(2 + hh, 192);   // head hh's C1 is done
+      named_bar(2 + hh, hh ? 128 : 192);   // head hh's C1 is done
       const float* L = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + (zw ? U_AT : U_A));
       float r[32];
       if (!zw) {
