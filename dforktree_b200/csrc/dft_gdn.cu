@@ -246,6 +246,8 @@ int dft_gdn_check(const dft_gdn_args* a) {
 
 bool dft_gdn_tc_applicable(const dft_gdn_args* a);
 int dft_gdn_tc_launch(const dft_gdn_args* a, int32_t* status, cudaStream_t st);
+bool dft_gdn_tc64_applicable(const dft_gdn_args* a);
+int dft_gdn_tc64_launch(const dft_gdn_args* a, int32_t* status, cudaStream_t st);
 
 extern "C" int dft_gdn_tree_verify(const dft_gdn_args* args, int32_t* dev_status, void* stream) {
   int rc = dft_gdn_check(args);
@@ -256,6 +258,9 @@ extern "C" int dft_gdn_tree_verify(const dft_gdn_args* args, int32_t* dev_status
   if (dft_gdn_tc_applicable(&a)) {
     rc = dft_gdn_tc_launch(&a, dev_status, s);
     if (rc != DFT_ERR_UNSUPPORTED || a.conv) return rc;   // tensor map refused: fall back to SIMT
+  } else if (dft_gdn_tc64_applicable(&a)) {
+    rc = dft_gdn_tc64_launch(&a, dev_status, s);
+    if (rc != DFT_ERR_UNSUPPORTED || a.conv) return rc;
   }
   if (a.conv) return DFT_ERR_UNSUPPORTED;   // the fused tree conv lives in the tcgen05 path
   if (a.N <= 32) return launch_simt<32>(a, dev_status, s);
