@@ -23,13 +23,15 @@
 // X lives in the state tile's slot once M1 has consumed the state.
 // Per unit:
 //   F  tree conv in place of the unit's bf16 tile (q, k, v: 3 + 64 rows),
-//      gathered by cp.async at the end of the previous unit
+//      gathered by cp.async and converted by warps 8-13 as soon as the
+//      previous unit's E1 has read v (alongside that unit's C2)
 //   N  L2 norms -> tf32 [k; q] operand (k rows 0-63, q rows 64-127), k_hat rows
 //   M0 D0 = [k; q] k^T     M1 D1 = S0 [k; q]^T
 //   C1 A = strict-anc(beta k.k^T e^{G_i-G_j}), PD = anc(q.k^T e^{G_i-G_j})
 //   C2 X by depth level, Z = PD X -> [X; Z] operand (3xTF32 hi / lo)
 //   E1 R = beta (v - e^G (k S0)) -> R^T hi / lo in TMEM (alongside C1 / C2)
-//   M2 D2 = R^T [X; Z]^T   -> vn^T, (Z R)^T
+//   M2 D2 = R^T [X; Z]^T   -> vn^T, (Z R)^T, issued once every warp has
+//      arrived on an mbarrier (operands ready) rather than at a CTA barrier
 //   E2 o = e^G (q S0) + Z R, vn -> global memory
 // Every wait is bounded (~1 s); on timeout the CTA raises DFT_DEV_TIMEOUT,
 // drains what it issued (bounded), frees TMEM and exits.
@@ -68,6 +70,7 @@ constexpr uint32_t kMaxSmem = 227 * 1024;
 
 struct Small {
   unsigned long long bar_s, bar_x, bar_m0, bar_m1, bar_m2, bar_dr;
+  unsigned long long bar_r;        // M2's operands ready: one arrival per warp
   uint32_t tmem_base;
   int abort;
   // per-unit inputs, double-buffered: unit u uses buffer (its ordinal) % 2
@@ -172,121 +175,118 @@ __device__ __forceinline__ void anc_masks64(const float* anc, int b, int N, int 
   }
 }
 
-// Per-unit masks and gates of unit u into buffer buf, by one warp per role.
-// Role 1: ancestor masks, conv taps and the depth-level order of the nodes;
-// role 0: gates g, beta, G = sum of g over the ancestors in ascending order
-// (tree_kernels.py:146-153), e^G.  Every global load is issued before any of
-// their values is used.
-template <bool CONV>
-__device__ __forceinline__ void prep_unit(const dft_gdn_args& a, const dft_gdn_conv_args& cv, Small& sm,
-                                          int32_t* status, int u, int buf, int role, int lane) {
+// Conv taps of unit u into buffer buf (one warp): the tile rows of taps 0..2
+// of every node, one byte each (tap 3 is the node itself).  Cheap, so that
+// the next unit's conv can start as soon as this unit's E1 is done.
+__device__ __forceinline__ void prep_taps(const dft_gdn_args& a, const dft_gdn_conv_args& cv, Small& sm,
+                                          int32_t* status, int u, int buf, int lane) {
+  const int N = a.N, b = u / a.Hv;
+  int64_t c4[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int n = lane + 32 * c;
+    if (n < N) {
+      const int64_t* ci = cv.cidx + ((int64_t)b * N + n) * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c4[c][j] = __ldg(reinterpret_cast<const long long*>(ci) + j);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int n = lane + 32 * c;
+    uint32_t packed = 0;
+    if (n < N) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        int64_t t = c4[c][j];
+        if (t < 0 || t >= 3 + N) {
+          raise_status(status, DFT_DEV_BAD_INDEX);
+          t = 3 + n;
+        }
+        packed |= (uint32_t)t << (8 * j);
+      }
+      if (c4[c][3] != 3 + n) raise_status(status, DFT_DEV_BAD_INDEX);   // tap 3 is the node itself
+    }
+    sm.taps[buf][n] = packed;
+  }
+  __syncwarp();
+}
+
+// Masks, depth-level order and gates of unit u into buffer buf (one warp):
+// ancestor masks; nodes ordered by depth (counting sort, stable by index);
+// gates g, beta, G = sum of g over the ancestors in ascending order
+// (tree_kernels.py:146-153), e^G, and G to aux_g.  Every global load is
+// issued before any of their values is used.
+__device__ __forceinline__ void prep_masks_gates(const dft_gdn_args& a, Small& sm, int u, int buf, int lane) {
   const int N = a.N, Hv = a.Hv;
   const int b = u / Hv, h = u % Hv;
-  uint32_t ra[2] = {0u, 0u}, rb[2] = {0u, 0u}, rd = 0u;
-  float dec = 0.f;
-  if (role == 0) {
+  uint32_t ra[2] = {0u, 0u}, rb[2] = {0u, 0u};
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int n = lane + 32 * c;
-      if (n < N) {
-        const int64_t ab = (int64_t)b * a.ab_sb + (int64_t)n * a.ab_sn + h;
-        ra[c] = ld_bits(a.a, a.ab_dtype, ab);
-        rb[c] = ld_bits(a.bg, a.ab_dtype, ab);
-      }
-    }
-    rd = ld_bits(a.dt_bias, a.dtb_dtype, h);
-    dec = a.neg_exp_A ? __ldg(a.neg_exp_A + h) : -expf(__ldg(a.A_log + h));
-  }
-  int64_t c4[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-  if (CONV && role == 1) {
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int n = lane + 32 * c;
-      if (n < N) {
-        const int64_t* ci = cv.cidx + ((int64_t)b * N + n) * 4;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) c4[c][j] = __ldg(reinterpret_cast<const long long*>(ci) + j);
-      }
+  for (int c = 0; c < 2; ++c) {
+    const int n = lane + 32 * c;
+    if (n < N) {
+      const int64_t ab = (int64_t)b * a.ab_sb + (int64_t)n * a.ab_sn + h;
+      ra[c] = ld_bits(a.a, a.ab_dtype, ab);
+      rb[c] = ld_bits(a.bg, a.ab_dtype, ab);
     }
   }
+  const uint32_t rd = ld_bits(a.dt_bias, a.dtb_dtype, h);
+  const float dec = a.neg_exp_A ? __ldg(a.neg_exp_A + h) : -expf(__ldg(a.A_log + h));
   unsigned long long m[2];
   anc_masks64(a.anc, b, N, lane, m[0], m[1]);
-  if (role == 1) {
-    sm.anc[buf][lane] = m[0];
-    sm.anc[buf][lane + 32] = m[1];
-    if (CONV) {
+  sm.anc[buf][lane] = m[0];
+  sm.anc[buf][lane + 32] = m[1];
+  // order[lstart[d] .. lstart[d + 1]) are the nodes of depth d; padding
+  // nodes (no mask) are left out
+  const int d0 = __popcll(m[0]) - 1, d1 = __popcll(m[1]) - 1;
+  int maxd = d0 > d1 ? d0 : d1;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int n = lane + 32 * c;
-        uint32_t packed = 0;
-        if (n < N) {
-#pragma unroll
-          for (int j = 0; j < 3; ++j) {
-            int64_t t = c4[c][j];
-            if (t < 0 || t >= 3 + N) {
-              raise_status(status, DFT_DEV_BAD_INDEX);
-              t = 3 + n;
-            }
-            packed |= (uint32_t)t << (8 * j);
-          }
-          if (c4[c][3] != 3 + n) raise_status(status, DFT_DEV_BAD_INDEX);   // tap 3 is the node itself
-        }
-        sm.taps[buf][n] = packed;
-      }
-    }
-    // nodes ordered by depth (counting sort, stable): order[lstart[d] ..
-    // lstart[d + 1]) are the nodes of depth d; padding nodes (no mask) are left out
-    const int d0 = __popcll(m[0]) - 1, d1 = __popcll(m[1]) - 1;
-    int maxd = d0 > d1 ? d0 : d1;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) maxd = max(maxd, __shfl_xor_sync(0xffffffffu, maxd, o));
-    const uint32_t lt = (1u << lane) - 1u;
-    int start = 0;
+  for (int o = 16; o > 0; o >>= 1) maxd = max(maxd, __shfl_xor_sync(0xffffffffu, maxd, o));
+  const uint32_t lt = (1u << lane) - 1u;
+  int start = 0;
 #pragma unroll 1
-    for (int d = 0; d <= maxd; ++d) {
-      const uint32_t b0 = __ballot_sync(0xffffffffu, d0 == d), b1 = __ballot_sync(0xffffffffu, d1 == d);
-      if (d0 == d) sm.order[buf][start + __popc(b0 & lt)] = (uint8_t)lane;
-      if (d1 == d) sm.order[buf][start + __popc(b0) + __popc(b1 & lt)] = (uint8_t)(lane + 32);
-      if (lane == 0) sm.lstart[buf][d] = (uint8_t)start;
-      start += __popc(b0) + __popc(b1);
-    }
-    if (lane == 0) {
-      sm.lstart[buf][maxd + 1] = (uint8_t)start;
-      sm.maxdepth[buf] = maxd;
-    }
-  } else {
-    float g[2], beta[2];
+  for (int d = 0; d <= maxd; ++d) {
+    const uint32_t b0 = __ballot_sync(0xffffffffu, d0 == d), b1 = __ballot_sync(0xffffffffu, d1 == d);
+    if (d0 == d) sm.order[buf][start + __popc(b0 & lt)] = (uint8_t)lane;
+    if (d1 == d) sm.order[buf][start + __popc(b0) + __popc(b1 & lt)] = (uint8_t)(lane + 32);
+    if (lane == 0) sm.lstart[buf][d] = (uint8_t)start;
+    start += __popc(b0) + __popc(b1);
+  }
+  if (lane == 0) {
+    sm.lstart[buf][maxd + 1] = (uint8_t)start;
+    sm.maxdepth[buf] = maxd;
+  }
+  float g[2], beta[2];
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      g[c] = 0.f;
-      beta[c] = 0.f;
-      if (lane + 32 * c < N) {
-        const float ar = bits_f32(ra[c], a.ab_dtype) + bits_f32(rd, a.dtb_dtype);
-        const float sp = ar > 20.f ? ar : logf(1.f + expf(fminf(ar, 20.f)));
-        g[c] = dec * sp;
-        beta[c] = 1.f / (1.f + expf(-bits_f32(rb[c], a.ab_dtype)));
-      }
+  for (int c = 0; c < 2; ++c) {
+    g[c] = 0.f;
+    beta[c] = 0.f;
+    if (lane + 32 * c < N) {
+      const float ar = bits_f32(ra[c], a.ab_dtype) + bits_f32(rd, a.dtb_dtype);
+      const float sp = ar > 20.f ? ar : logf(1.f + expf(fminf(ar, 20.f)));
+      g[c] = dec * sp;
+      beta[c] = 1.f / (1.f + expf(-bits_f32(rb[c], a.ab_dtype)));
     }
-    float G[2] = {0.f, 0.f};
+  }
+  float G[2] = {0.f, 0.f};
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
+  for (int hf = 0; hf < 2; ++hf) {
 #pragma unroll 8
-      for (int j = 0; j < 32; ++j) {
-        const float gj = __shfl_sync(0xffffffffu, g[hf], j);
-        const int bit = 32 * hf + j;
+    for (int j = 0; j < 32; ++j) {
+      const float gj = __shfl_sync(0xffffffffu, g[hf], j);
+      const int bit = 32 * hf + j;
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-          if ((m[c] >> bit) & 1ull) G[c] += gj;
-      }
+      for (int c = 0; c < 2; ++c)
+        if ((m[c] >> bit) & 1ull) G[c] += gj;
     }
+  }
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int n = lane + 32 * c;
-      sm.G[buf][n] = G[c];
-      sm.beta[buf][n] = beta[c];
-      sm.eG[buf][n] = expf(G[c]);
-      if (a.aux_g && n < N) a.aux_g[(int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh + n] = G[c];
-    }
+  for (int c = 0; c < 2; ++c) {
+    const int n = lane + 32 * c;
+    sm.G[buf][n] = G[c];
+    sm.beta[buf][n] = beta[c];
+    sm.eG[buf][n] = expf(G[c]);
+    if (a.aux_g && n < N) a.aux_g[(int64_t)b * a.ag_sb + (int64_t)h * a.ag_sh + n] = G[c];
   }
   __syncwarp();
 }
@@ -312,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kConvThreads = 64 * 3;                 // channel pairs of q, k, v
   const uint32_t bar_s = smem_u32(&sm.bar_s), bar_x = smem_u32(&sm.bar_x), bar_m0 = smem_u32(&sm.bar_m0);
   const uint32_t bar_m1 = smem_u32(&sm.bar_m1), bar_m2 = smem_u32(&sm.bar_m2), bar_dr = smem_u32(&sm.bar_dr);
+  const uint32_t bar_r = smem_u32(&sm.bar_r);
   // lane 0 of the last warp issues every TMA and MMA; the warp reconverges
   // (__syncwarp) after each control block, so that every CTA barrier is
   // reached by whole warps
@@ -326,6 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_m1, 1);
       mbar_init(bar_m2, 1);
       mbar_init(bar_dr, 1);
+      mbar_init(bar_r, kThreads / 32);
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
       sm.abort = 0;
       sm.s_issued = 0;
@@ -373,11 +375,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
 
-  // conv: thread -> channel pair (part tid / 64, channels 2 (tid % 64) + {0, 1});
-  // its weights, bias and conv state are fetched one unit ahead (raw bits)
-  const int cpart = tid >> 6;
-  const int cpair = (tid & 63) * 2;
-  const bool conv_thr = CONV && tid < kConvThreads;
+  // conv: warps 8-13, thread 256 + t -> channel pair (part t / 64, channels
+  // 2 (t % 64) + {0, 1}); its weights, bias and conv state are fetched one unit
+  // ahead (raw bits).  The next unit's gather and conv run once this unit's E1
+  // has read v, alongside C2.
+  const int ctid = tid - 256;
+  const int cpart = ctid >> 6;
+  const int cpair = (ctid & 63) * 2;
+  const bool conv_thr = CONV && tid >= 256 && ctid < kConvThreads;
   uint4 pw = make_uint4(0u, 0u, 0u, 0u);
   uint32_t pb = 0u;
   unsigned short ps[6] = {0, 0, 0, 0, 0, 0};   // conv state (tap j, channel e) at 2 j + e
@@ -397,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   };
   if (conv_thr && (int)blockIdx.x < units) load_conv(blockIdx.x);
-  if (warp == 14 && (int)blockIdx.x < units) prep_unit<CONV>(a, ta.cv, sm, status, blockIdx.x, 0, 1, lane);
+  if (CONV && warp == 14 && (int)blockIdx.x < units) prep_taps(a, ta.cv, sm, status, blockIdx.x, 0, lane);
   // activations (x or y, a, bg) and every global write come after the
   // previous kernel has completed; the next launch may then be scheduled
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -406,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     issue_act(blockIdx.x);
     x_issued = 1;
   }
-  if (warp == 12 && (int)blockIdx.x < units) prep_unit<CONV>(a, ta.cv, sm, status, blockIdx.x, 0, 0, lane);
+  if (warp == 14 && (int)blockIdx.x < units) prep_masks_gates(a, sm, blockIdx.x, 0, lane);
 
   // tree conv in place (fc1_conv.py:8-27) of unit cu from taps buffer cbuf,
   // by the conv threads: one channel pair per thread, nodes from last to first
@@ -459,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const unsigned char* xb = static_cast<const unsigned char*>(ta.cv.x) + (int64_t)nb * ta.cv.x_sb * 2;
 #pragma unroll 4
     for (int i = 0; i < 16; ++i) {
-      const int id = tid + kConvThreads * i;            // 0 .. 3071
+      const int id = ctid + kConvThreads * i;           // 0 .. 3071
       const int p = id >> 10, row = (id >> 4) & 63, c16 = id & 15;
       const bool in = row < N;
       const unsigned char* src =
@@ -579,10 +584,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     }
-    // ------------------------------------------------ the next unit's masks and gates (warps 12, 14)
-    if (warp == 12 || warp == 14) {
+    // ------------------------------------------------ the next unit's conv taps (warp 14)
+    if (CONV && warp == 14) {
       const int nu = u + gridDim.x;
-      if (nu < units) prep_unit<CONV>(a, ta.cv, sm, status, nu, cb ^ 1, warp == 14 ? 1 : 0, lane);
+      if (nu < units) prep_taps(a, ta.cv, sm, status, nu, cb ^ 1, lane);
     }
     // ------------------------------------------------ C1, C2 (warps 0-7)
     if (warp < 8) {
@@ -613,11 +618,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       named_bar(2, 256);   // A and PD written
       // C2: X by depth level into the state slot (free once M1 has retired;
-      // [k; q] is then free for the [X; Z] operand as well)
+      // [k; q] is then free for the [X; Z] operand as well).  Warp w takes
+      // rows w, w + 8, .. of a level; lane c owns columns c and c + 32.  Right
+      // after its X row n the warp forms Z row n = sum over n's ancestors-or-self
+      // j of PD[n][j] X[j] (rows of earlier levels, and its own X row in
+      // registers) and writes both as [X; Z] operand rows n and 64 + n (hi / lo
+      // tf32 split; one 128-byte row per K-block and store).
       if (!mbar_wait(bar_m1, ph)) atomicExch(&sm.abort, 1);
       float* X = reinterpret_cast<float*>(smem + OFF_S0);           // X[i][c] at i * 64 + c
       const float* A = reinterpret_cast<const float*>(smem + OFF_U + U_A);
       const float* PD = reinterpret_cast<const float*>(smem + OFF_U + U_PD);
+      unsigned char* xzh = smem + OFF_KQ;
+      unsigned char* xzl = xzh + 32768;
+      auto put_row = [&](int row, float v0, float v1) {
+#pragma unroll
+        for (int kb2 = 0; kb2 < 2; ++kb2) {
+          const float val = kb2 ? v1 : v0;
+          const uint32_t off = (uint32_t)(kb2 * 16384 + row * 128 + ((((lane >> 2) ^ row) & 7) << 4) + (lane & 3) * 4);
+          const float hi = tf32_rna(val);
+          *reinterpret_cast<float*>(xzh + off) = hi;
+          *reinterpret_cast<float*>(xzl + off) = tf32_rna(val - hi);
+        }
+      };
+      // operand rows of padding nodes are zero
+      for (int n = N + warp; n < kNP; n += 8) {
+        put_row(n, 0.f, 0.f);
+        put_row(64 + n, 0.f, 0.f);
+      }
       const int maxd = sm.maxdepth[cb];
 #pragma unroll 1
       for (int d = 0; d <= maxd; ++d) {
@@ -627,7 +654,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int i = sm.order[cb][k];
           float x0 = lane == i ? 1.f : 0.f, x1 = lane + 32 == i ? 1.f : 0.f;
           // strict ancestors, ascending (the rows of the previous levels)
-          unsigned long long msk = sm.anc[cb][i] & ((1ull << i) - 1ull);
+          const unsigned long long sanc = sm.anc[cb][i] & ((1ull << i) - 1ull);
+          unsigned long long msk = sanc;
 #pragma unroll 1
           while (msk) {
             const int m = __ffsll((long long)msk) - 1;
@@ -638,45 +666,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           X[i * 64 + lane] = x0;
           X[i * 64 + 32 + lane] = x1;
-        }
-        named_bar(3, 256);   // level d written
-      }
-      // [X; Z] operand rows (hi / lo tf32 split): row n = X row n, row 64 + n
-      // = Z row n = sum over n's ancestors-or-self j of PD[n][j] X[j]; rows of
-      // padding nodes are zero.  Lane c writes element c and c + 32 of a row
-      // (K-blocks 0 and 1): one 128-byte row per K-block and store
-      unsigned char* xzh = smem + OFF_KQ;
-      unsigned char* xzl = xzh + 32768;
-#pragma unroll 1
-      for (int n = warp; n < kNP; n += 8) {
-        float xv[2] = {0.f, 0.f}, zv[2] = {0.f, 0.f};
-        if (n < N) {
-          xv[0] = X[n * 64 + lane];
-          xv[1] = X[n * 64 + 32 + lane];
-          unsigned long long msk = sm.anc[cb][n] & ((2ull << n) - 1ull);
+          float z0 = 0.f, z1 = 0.f;
+          msk = sanc;
 #pragma unroll 1
           while (msk) {
             const int j = __ffsll((long long)msk) - 1;
             msk &= msk - 1ull;
-            const float pj = PD[sq64(n, j)];
-            zv[0] = fmaf(pj, X[j * 64 + lane], zv[0]);
-            zv[1] = fmaf(pj, X[j * 64 + 32 + lane], zv[1]);
+            const float pj = PD[sq64(i, j)];
+            z0 = fmaf(pj, X[j * 64 + lane], z0);
+            z1 = fmaf(pj, X[j * 64 + 32 + lane], z1);
           }
+          const float pii = PD[sq64(i, i)];
+          z0 = fmaf(pii, x0, z0);
+          z1 = fmaf(pii, x1, z1);
+          put_row(i, x0, x1);
+          put_row(64 + i, z0, z1);
         }
-#pragma unroll
-        for (int kb2 = 0; kb2 < 2; ++kb2) {
-          const int c = lane;   // element c of K-block kb2 (node 32 kb2 + c)
-#pragma unroll
-          for (int part = 0; part < 2; ++part) {
-            const int row = part ? 64 + n : n;
-            const float val = part ? zv[kb2] : xv[kb2];
-            const uint32_t off = (uint32_t)(kb2 * 16384 + row * 128 + ((((c >> 2) ^ row) & 7) << 4) + (c & 3) * 4);
-            const float hi = tf32_rna(val);
-            *reinterpret_cast<float*>(xzh + off) = hi;
-            *reinterpret_cast<float*>(xzl + off) = tf32_rna(val - hi);
-          }
-        }
+        named_bar(3, 256);   // level d written
       }
+      // the operand rows, for the tensor cores; then this warp's arrival for M2
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_r);
     }
     // ------------------------------------------------ E1 (warps 8-15), alongside C1 / C2
     // R = beta (v - e^G (k S0)) by the thread owning TMEM lane v; warps 8-11
@@ -713,17 +724,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st16(tmem + lanes + COL_RT + 32 * nh + 16 * c16, hi);
         tmem_st16(tmem + lanes + COL_RT + 64 + 32 * nh + 16 * c16, lo);
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_r);
+      // every E1 warp has read v and the next unit's taps are prepared (warp 14):
+      // the activation tile takes the next unit's rows (warps 8-13), while
+      // warp 14 prepares the next unit's masks, depth order and gates (first
+      // read by that unit's C1)
+      named_bar(4, 256);
+      const int nu = u + gridDim.x;
+      if (conv_thr && nu < units) {
+        gather_tile(nu);
+        gather_wait();
+        do_conv(nu, cb ^ 1);
+      }
+      if (warp == 14 && nu < units) prep_masks_gates(a, sm, nu, cb ^ 1, lane);
     }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (sm.abort) break;
     if (ctl_warp) {
       if (lane == 0) {
         const int nu = u + gridDim.x;
+        // M2's operands: [X; Z] (warps 0-7) and R^T (warps 8-15)
+        if (!mbar_wait(bar_r, ph)) atomicExch(&sm.abort, 1);
+        tc_fence_after();
         if (!CONV && nu < units) {
-          issue_act(nu);
+          issue_act(nu);   // the tile is consumed (E1 has read v)
           ++x_issued;
         }
         // M2: D2 = R^T [X; Z]^T, 3xTF32 (hi.hi + hi.lo + lo.hi); K = 64 nodes in
@@ -741,8 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) mma_tf32_ts(dcol, al + 8 * ks, bh0 + 1024 * (ks >> 2) + 2 * (ks & 3), id2, 1);
         mma_commit(bar_m2);
-        // the state slot held X, consumed before the barrier above: it takes
-        // the next unit's state
+        // X (in the state slot) is consumed: the slot takes the next unit's state
         if (nu < units) {
           issue_state(nu);
           ++s_issued;
@@ -779,15 +802,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-      }
-    }
-    // ------------------------------------------------ the next unit's tile and conv (warps 0-5)
-    if (conv_thr) {
-      const int nu = u + gridDim.x;
-      if (nu < units) {
-        gather_tile(nu);
-        gather_wait();
-        do_conv(nu, cb ^ 1);
       }
     }
     tc_fence_before();
