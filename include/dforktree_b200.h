@@ -252,9 +252,10 @@ DFT_API int dft_conv_commit(const dft_conv_commit_args* a, int32_t* dev_status, 
  * With `conv` set, y is not read: the tree conv of fc1_conv.py:8-27 is
  * computed from the pre-conv inputs inside the verifier (the window taps
  * are not written; dft_tree_conv does that for the drop-in hook).  The fused
- * conv runs on the tensor-core path only (N <= 32, Dk = Dv = 128, Hv / Hk in
- * {1, 2}, bfloat16 x, conv state, weights and o, 16-byte aligned rows); others
- * return DFT_ERR_UNSUPPORTED and take dft_tree_conv + this call on y. */
+ * conv runs on the tensor-core paths only (N <= 32 with Hv / Hk in {1, 2}, or
+ * 32 < N <= 64 with any Hv / Hk; Dk = Dv = 128, bfloat16 x, conv state,
+ * weights and o, 16-byte aligned rows); others return DFT_ERR_UNSUPPORTED and
+ * take dft_tree_conv + this call on y. */
 typedef struct {
   const void* x; int32_t x_dtype; int64_t x_sb, x_sn;   /* pre-conv (b, n, col), col stride 1 */
   const void* conv_state; int32_t cs_dtype; int64_t cs_ss, cs_sc, cs_st;
