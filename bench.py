@@ -702,6 +702,47 @@ def run_profile_attention(args):
         raise RuntimeError(f"tree attention raised device status {w.device_status()}")
 
 
+def run_profile_stage(args):
+    """--profile-n64 / --profile-pmi ORDER: W + K launches of one stage alone at
+    the bench's batch (for ncu); prints nothing.  n64: tree conv + verify of the
+    plugin's default 64-node tree on two alternating layers; pmi: the dense
+    PMI tensor of that n-gram order over the bench's scored logits, with a
+    table that also carries 4M quadgram rows."""
+    import torch
+    from dforktree_b200 import build as B
+    from dforktree_b200 import kernels as K
+    from dforktree_b200 import synth
+    from dforktree_b200 import workload as WL
+    from dforktree_b200.cycle import CycleConfig, DraftTreeCycle
+    from dforktree_b200.ngram_gpu import load_npz_arrays
+    B.build()
+    dev = torch.device("cuda", 0)
+    quad = 4_000_000 if args.profile_pmi else 0
+    table = K.Table(load_npz_arrays(synth.make_ngram_table(V, 2_000_000, 8_000_000, seed=0, n_quad=quad)),
+                    beta3=60.0, device=dev)
+    if args.profile_n64:
+        cfg = CycleConfig(B=args.batch, layers=2, N=64)
+        cyc = DraftTreeCycle(cfg, table, dev, seed=7)
+        inp = WL.cycle_inputs(cfg, dev, seed=99)
+        cyc.build(inp["logits"], inp["root"], inp["pre1"])
+        for _ in range(args.warmup + args.steps):
+            for l in range(2):
+                cyc.verify_layer(l, inp["x"][l], inp["a"][l], inp["b"][l])
+        torch.cuda.synchronize()
+        status = int(cyc.status.item())
+    else:
+        cfg = CycleConfig(B=args.batch, layers=1)
+        inp = WL.cycle_inputs(cfg, dev, seed=1234)
+        _, ids, _ = K.score(inp["logits"])
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        for _ in range(args.warmup + args.steps):
+            K.pmi_dense(table, ids, inp["root"], inp["pre1"], status=st, order=args.profile_pmi)
+        torch.cuda.synchronize()
+        status = int(st.item())
+    if status:
+        raise RuntimeError(f"profiled stage raised device status {status}")
+
+
 def _traffic():
     """DRAM bytes per launch of the bench kernels from the committed ncu summary."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
@@ -893,9 +934,16 @@ def main():
     ap.add_argument("--profile", action="store_true", help="only W + K plain cycles (for ncu); prints nothing")
     ap.add_argument("--profile-attn", action="store_true",
                     help="only W + K tree-attention layers at the bench shape (for ncu); prints nothing")
+    ap.add_argument("--profile-n64", action="store_true",
+                    help="only W + K 64-node tree conv + verify launches at the bench's batch (for ncu); prints nothing")
+    ap.add_argument("--profile-pmi", type=int, default=0, choices=(0, 2, 3, 4),
+                    help="only W + K dense-PMI launches of this n-gram order at the bench's batch (for ncu)")
     args = ap.parse_args()
     if args.profile_attn:
         run_profile_attention(args)
+        return
+    if args.profile_n64 or args.profile_pmi:
+        run_profile_stage(args)
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
