@@ -503,7 +503,12 @@ def run_ours(args, rank, world, local_rank):
         "gdn_verify_GBps": verify_bytes / (verify_launch_ms / 1e3) / 1e9,
         "gdn_commit_GBps": commit_bytes / (commit_launch_ms / 1e3) / 1e9,
         "mean_accept_len": mean_acc,
+        # the whole cycle against the roofline: every stage's algorithmic bytes
+        # (score + build, 24 verifies, the commit) over the measured cycle time
+        "request_cycles_per_s": Bt * args.steps / (ms / 1e3),
+        "cycle_GBps": (Bt * SCORE_BYTES + verify_bytes * cfg.layers + commit_bytes) / (ms / args.steps / 1e3) / 1e9,
     }
+    per_kernel["cycle_hbm_frac"] = per_kernel["cycle_GBps"] / hbm
     if attn is not None:
         per_kernel["tree_attn_ms_per_layer"] = attn
         per_kernel["tree_attn_GBps"] = Bt * ATTN_BYTES / (attn / 1e3) / 1e9
