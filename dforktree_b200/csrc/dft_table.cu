@@ -622,7 +622,7 @@ __device__ __forceinline__ uint4 fp_round2(const Slot* tab, const uint8_t* fp, u
 // times.
 constexpr int kM = 16;
 
-__global__ void __launch_bounds__(256) pmi_dense_kernel(TableView t, int S, const int32_t* __restrict__ ids,
+__global__ void __launch_bounds__(256, 3) pmi_dense_kernel(TableView t, int S, const int32_t* __restrict__ ids,
                                                         const int64_t* __restrict__ root,
                                                         const int64_t* __restrict__ pre1, float* __restrict__ T,
                                                         int32_t* st) {
@@ -661,31 +661,38 @@ __global__ void __launch_bounds__(256) pmi_dense_kernel(TableView t, int S, cons
   __syncthreads();
   float* Tout = T + ((int64_t)req * (S - 1) + tstep) * (kM * kM * kM);
   const int rows = tstep == 0 ? 1 : 16;       // row r of this thread's triples is i = r
-  long long q[16];
-  uint2 w[16];
-#pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    int e = tid + 256 * r;
-    int i = e >> 8, j = (e >> 4) & 15, l = e & 15;
-    long long a = sa[i], b = sb[j];
-    q[r] = (r < rows && a >= 0 && b >= 0 && t.has_trip) ? (a * V + b) * V + sc[l] : -1;
-    w[r] = fp_round1(t.trip_fp, t.trip_mask, q[r], pol);
-  }
+  // two rounds of 8 probes per thread (every first fingerprint load of a round
+  // in flight): 8 rather than 16 keeps the kernel at three CTAs per SM
   float v0 = 0.f;
 #pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    int e = tid + 256 * r;
-    int i = e >> 8, j = (e >> 4) & 15, l = e & 15;
-    float v;
-    if (r < rows) {
-      const uint4 hit = fp_round2(t.trip, t.trip_fp, t.trip_mask, q[r], w[r], st);
-      const float p3 = p3_from(__uint_as_float(hit.z), s_nab[i * 16 + j], s_p2[j * 16 + l], t.beta3);
-      v = pmi_from(p3, s_lpn[l], t.clip);
-      if (r == 0) v0 = v;
-    } else {
-      v = v0;   // t = 0: row i equals row 0
+  for (int r0 = 0; r0 < 16; r0 += 8) {
+    long long q[8];
+    uint2 w[8];
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) {
+      const int r = r0 + rr;
+      int e = tid + 256 * r;
+      int i = e >> 8, j = (e >> 4) & 15, l = e & 15;
+      long long a = sa[i], b = sb[j];
+      q[rr] = (r < rows && a >= 0 && b >= 0 && t.has_trip) ? (a * V + b) * V + sc[l] : -1;
+      w[rr] = fp_round1(t.trip_fp, t.trip_mask, q[rr], pol);
     }
-    Tout[e] = v;
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) {
+      const int r = r0 + rr;
+      int e = tid + 256 * r;
+      int i = e >> 8, j = (e >> 4) & 15, l = e & 15;
+      float v;
+      if (r < rows) {
+        const uint4 hit = fp_round2(t.trip, t.trip_fp, t.trip_mask, q[rr], w[rr], st);
+        const float p3 = p3_from(__uint_as_float(hit.z), s_nab[i * 16 + j], s_p2[j * 16 + l], t.beta3);
+        v = pmi_from(p3, s_lpn[l], t.clip);
+        if (r == 0) v0 = v;
+      } else {
+        v = v0;   // t = 0: row i equals row 0
+      }
+      Tout[e] = v;
+    }
   }
 }
 
