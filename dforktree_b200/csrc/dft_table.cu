@@ -733,7 +733,7 @@ struct P4Smem {
   int i3[kM * kM * kM];
 };
 
-__global__ void __launch_bounds__(kP4Threads) pmi_dense4_kernel(TableView t, int S, const int32_t* __restrict__ ids,
+__global__ void __launch_bounds__(kP4Threads, 2) pmi_dense4_kernel(TableView t, int S, const int32_t* __restrict__ ids,
                                                                 const int64_t* __restrict__ root,
                                                                 const int64_t* __restrict__ pre1,
                                                                 float* __restrict__ T, int32_t* st) {
@@ -776,46 +776,49 @@ __global__ void __launch_bounds__(kP4Threads) pmi_dense4_kernel(TableView t, int
     }
   }
   __syncthreads();
-  {  // phase 2: 8 trigram + 8 context-trigram probes per thread
-    long long q[16];
-    uint2 w[16];
+  {  // phase 2: 8 trigram probes, then 8 context-trigram probes per thread
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      long long q[8];
+      uint2 w[8];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const int e = tid + kP4Threads * (r & 7);  // 0 .. 4095
-      const int hi = e >> 8, mid = (e >> 4) & 15, lo = e & 15;
-      if (r < 8) {  // (a_hi, b_mid, c_lo)
-        const long long a = sm.sa[hi], b = sm.sb[mid];
-        q[r] = (hi < ja && a >= 0 && b >= 0 && t.has_trip) ? (a * V + b) * V + sm.sc[lo] : -1;
-      } else {      // (z_hi, a_mid, b_lo)
-        const long long z = sm.sz[hi], a = sm.sa[mid], b = sm.sb[lo];
-        q[r] = (hi < hz && mid < ja && z >= 0 && a >= 0 && b >= 0 && t.has_trip) ? (z * V + a) * V + b : -1;
+      for (int r = 0; r < 8; ++r) {
+        const int e = tid + kP4Threads * r;  // 0 .. 4095
+        const int hi = e >> 8, mid = (e >> 4) & 15, lo = e & 15;
+        if (half == 0) {  // (a_hi, b_mid, c_lo)
+          const long long a = sm.sa[hi], b = sm.sb[mid];
+          q[r] = (hi < ja && a >= 0 && b >= 0 && t.has_trip) ? (a * V + b) * V + sm.sc[lo] : -1;
+        } else {          // (z_hi, a_mid, b_lo)
+          const long long z = sm.sz[hi], a = sm.sa[mid], b = sm.sb[lo];
+          q[r] = (hi < hz && mid < ja && z >= 0 && a >= 0 && b >= 0 && t.has_trip) ? (z * V + a) * V + b : -1;
+        }
+        w[r] = fp_round1(t.trip_fp, t.trip_mask, q[r], pol);
       }
-      w[r] = fp_round1(t.trip_fp, t.trip_mask, q[r], pol);
-    }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const int e = tid + kP4Threads * (r & 7);
-      const int hi = e >> 8, mid = (e >> 4) & 15, lo = e & 15;
-      const uint4 s = fp_round2(t.trip, t.trip_fp, t.trip_mask, q[r], w[r], st);
-      if (r < 8) {
-        if (hi < ja) sm.p3[e] = p3_from(__uint_as_float(s.z), sm.nab[hi * 16 + mid], sm.p2[mid * 16 + lo], t.beta3);
-      } else if (hi < hz && mid < ja) {
-        const bool hit = q[r] >= 0 && slot_key(s) == static_cast<unsigned long long>(q[r]);
-        const int i3 = hit ? (int)s.w : -1;
-        sm.i3[e] = i3;
-        sm.n4[e] = (hit && t.has_quad) ? __ldg(t.n4c + i3) : 0.f;
+      for (int r = 0; r < 8; ++r) {
+        const int e = tid + kP4Threads * r;
+        const int hi = e >> 8, mid = (e >> 4) & 15, lo = e & 15;
+        const uint4 s = fp_round2(t.trip, t.trip_fp, t.trip_mask, q[r], w[r], st);
+        if (half == 0) {
+          if (hi < ja) sm.p3[e] = p3_from(__uint_as_float(s.z), sm.nab[hi * 16 + mid], sm.p2[mid * 16 + lo], t.beta3);
+        } else if (hi < hz && mid < ja) {
+          const bool hit = q[r] >= 0 && slot_key(s) == static_cast<unsigned long long>(q[r]);
+          const int i3 = hit ? (int)s.w : -1;
+          sm.i3[e] = i3;
+          sm.n4[e] = (hit && t.has_quad) ? __ldg(t.n4c + i3) : 0.f;
+        }
       }
     }
   }
   __syncthreads();
   float* Tout = T + ((int64_t)req * (S - 1) + tstep) * (kM * kM * kM * kM);
   const int hmask = hz > 1 ? 15 : 0, jmask = ja > 1 ? 15 : 0;
-  // phase 3: 128 quadgrams per thread in batches of 16
-  for (int r0 = 0; r0 < 128; r0 += 16) {
-    long long q[16];
-    uint2 w[16];
+  // phase 3: 128 quadgrams per thread in batches of 8 (two CTAs per SM)
+  for (int r0 = 0; r0 < 128; r0 += 8) {
+    long long q[8];
+    uint2 w[8];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
+    for (int r = 0; r < 8; ++r) {
       const int e = tid + kP4Threads * (r0 + r);
       const int h = (e >> 12) & hmask, j = (e >> 8) & jmask, k = (e >> 4) & 15, l = e & 15;
       const int i3 = sm.i3[(h * 16 + j) * 16 + k];
@@ -823,7 +826,7 @@ __global__ void __launch_bounds__(kP4Threads) pmi_dense4_kernel(TableView t, int
       w[r] = fp_round1(t.quad_fp, t.quad_mask, q[r], pol);
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
+    for (int r = 0; r < 8; ++r) {
       const int e = tid + kP4Threads * (r0 + r);
       const int h = (e >> 12) & hmask, j = (e >> 8) & jmask, k = (e >> 4) & 15, l = e & 15;
       const uint4 s = fp_round2(t.quad, t.quad_fp, t.quad_mask, q[r], w[r], st);
