@@ -223,36 +223,92 @@ __global__ void __launch_bounds__(P) beam_kernel(BeamArgs a) {
     c_sc[tid] = sc_c;
     c_lv[tid] = lv_c;
     c_fl[tid] = fl_c;
-    // bitonic sort, descending by key, ties by ascending flat index
-#pragma unroll 1
-    for (int size = 2; size <= P; size <<= 1) {
-#pragma unroll 1
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        float ok_;
-        int oi_;
-        if (stride >= 32) {
-          sk[tid] = key;
-          si[tid] = idx;
-          __syncthreads();
-          ok_ = sk[tid ^ stride];
-          oi_ = si[tid ^ stride];
-          __syncthreads();
-        } else {
-          ok_ = __shfl_xor_sync(0xffffffffu, key, stride);
-          oi_ = __shfl_xor_sync(0xffffffffu, idx, stride);
-        }
-        const bool lower = (tid & stride) == 0;
-        const bool dir = (tid & size) == 0;
-        const bool mine_first = before(key, idx, ok_, oi_);
-        if ((lower == dir) ? !mine_first : mine_first) {
-          key = ok_;
-          idx = oi_;
+    if (W <= 32) {
+      // top 32 of the P keys (descending, ties by ascending flat index) without
+      // a full sort: every warp sorts its 32 keys (shuffle bitonic), then
+      // pairs of sorted lists merge by halves -- max(A[i], B[31 - i]) holds the
+      // 32 best of A and B as a bitonic sequence, five shuffle stages sort it
+      // -- over log2(P / 32) rounds with one barrier each
+#pragma unroll
+      for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          const float ok_ = __shfl_xor_sync(0xffffffffu, key, stride);
+          const int oi_ = __shfl_xor_sync(0xffffffffu, idx, stride);
+          const bool lower = (lane & stride) == 0;
+          const bool dir = size == 32 || (lane & size) == 0;
+          const bool mine_first = before(key, idx, ok_, oi_);
+          if ((lower == dir) ? !mine_first : mine_first) {
+            key = ok_;
+            idx = oi_;
+          }
         }
       }
+      const int wid = tid >> 5;
+#pragma unroll 1
+      for (int span = 1; span < P / 32; span <<= 1) {
+        sk[tid] = key;
+        si[tid] = idx;
+        __syncthreads();
+        if ((wid & (2 * span - 1)) == 0) {
+          const int pj = ((wid + span) << 5) + (31 - lane);
+          const float ok_ = sk[pj];
+          const int oi_ = si[pj];
+          if (!before(key, idx, ok_, oi_)) {
+            key = ok_;
+            idx = oi_;
+          }
+#pragma unroll
+          for (int stride = 16; stride > 0; stride >>= 1) {
+            const float ok2 = __shfl_xor_sync(0xffffffffu, key, stride);
+            const int oi2 = __shfl_xor_sync(0xffffffffu, idx, stride);
+            const bool lower = (lane & stride) == 0;
+            const bool mine_first = before(key, idx, ok2, oi2);
+            if (lower ? !mine_first : mine_first) {
+              key = ok2;
+              idx = oi2;
+            }
+          }
+        }
+        __syncthreads();
+      }
+      if (tid < 32) {
+        sk[tid] = key;
+        si[tid] = idx;
+      }
+      __syncthreads();
+    } else {
+      // bitonic sort, descending by key, ties by ascending flat index
+#pragma unroll 1
+      for (int size = 2; size <= P; size <<= 1) {
+#pragma unroll 1
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          float ok_;
+          int oi_;
+          if (stride >= 32) {
+            sk[tid] = key;
+            si[tid] = idx;
+            __syncthreads();
+            ok_ = sk[tid ^ stride];
+            oi_ = si[tid ^ stride];
+            __syncthreads();
+          } else {
+            ok_ = __shfl_xor_sync(0xffffffffu, key, stride);
+            oi_ = __shfl_xor_sync(0xffffffffu, idx, stride);
+          }
+          const bool lower = (tid & stride) == 0;
+          const bool dir = (tid & size) == 0;
+          const bool mine_first = before(key, idx, ok_, oi_);
+          if ((lower == dir) ? !mine_first : mine_first) {
+            key = ok_;
+            idx = oi_;
+          }
+        }
+      }
+      sk[tid] = key;
+      si[tid] = idx;
+      __syncthreads();
     }
-    sk[tid] = key;
-    si[tid] = idx;
-    __syncthreads();
     // new beams (tree_ops.py:35-43)
     float n_sc = 0.f, n_key = 0.f;
     int n_fl = 0, n_lv = 0, n_pc = 0, n_ppc = 0, n_al = 0, p_ = 0, c_ = 0;
