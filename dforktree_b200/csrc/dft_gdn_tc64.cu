@@ -37,6 +37,7 @@
 // drains what it issued (bounded), frees TMEM and exits.
 #include "dft_common.cuh"
 #include "dft_tc.cuh"
+#include "dft_gdn_tile.cuh"
 
 #include <cuda.h>
 
@@ -45,6 +46,7 @@
 
 using namespace dft;
 using namespace dft::tc;
+using namespace dft::gtile;
 
 namespace {
 
@@ -91,41 +93,7 @@ static_assert(sizeof(Small) <= kSmallBytes, "small region");
 // XOR-swizzled by i mod 16
 __device__ __forceinline__ int sq64(int i, int j) { return i * 64 + ((((j >> 2) ^ i) & 15) << 2) + (j & 3); }
 
-__device__ __forceinline__ float tf32_rna(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
 
-// raw element bits (fp32, or bf16 / f16 in the low half) and their value
-__device__ __forceinline__ uint32_t ld_bits(const void* p, int dtype, int64_t i) {
-  if (dtype == DFT_F32) return __ldg(reinterpret_cast<const uint32_t*>(p) + i);
-  return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p) + i);
-}
-__device__ __forceinline__ float bits_f32(uint32_t v, int dtype) {
-  if (dtype == DFT_F32) return __uint_as_float(v);
-  if (dtype == DFT_BF16) return __uint_as_float(v << 16);
-  return __half2float(__ushort_as_half((unsigned short)v));
-}
-
-// global loads the compiler keeps where they are written (prefetch one unit ahead)
-__device__ __forceinline__ uint4 ldg_keep_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-  return r;
-}
-__device__ __forceinline__ uint32_t ldg_keep_u32(const void* p) {
-  uint32_t r;
-  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
-  return r;
-}
-__device__ __forceinline__ unsigned short ldg_keep_u16(const void* p) {
-  unsigned short r;
-  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
-  return r;
-}
-__device__ __forceinline__ uint32_t ld_s32(const unsigned char* p) { return *reinterpret_cast<const uint32_t*>(p); }
-__device__ __forceinline__ void st_s32(unsigned char* p, uint32_t v) { *reinterpret_cast<uint32_t*>(p) = v; }
 
 // four consecutive bf16 channels of a tile row
 __device__ __forceinline__ float4 ld4_bf16(const unsigned char* p) {
@@ -134,10 +102,6 @@ __device__ __forceinline__ float4 ld4_bf16(const unsigned char* p) {
                      __uint_as_float(u.y & 0xFFFF0000u));
 }
 
-struct TcArgs {
-  dft_gdn_args g;
-  dft_gdn_conv_args cv;
-};
 
 // first channel of activation part p (q and k of k-head hk, v of v-head h)
 __device__ __forceinline__ int part_channel(int p, int h, int hk, int Hk) {
@@ -830,36 +794,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda at link time)
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
-
-inline bool al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 // dynamic shared memory of one launch: fixed regions + activation tile + alignment slack
 uint32_t smem_bytes(bool conv) { return OFF_ACT + 3u * (uint32_t)((conv ? 3 : 0) + kNP) * kD * 2 + 1024; }
