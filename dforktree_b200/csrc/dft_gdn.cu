@@ -72,8 +72,8 @@ __global__ void __launch_bounds__(kThreads) gdn_verify_simt(dft_gdn_args a, int3
                        load_any(a.y, a.y_dtype, r + 2 * KD + h * kD + d + 2),
                        load_any(a.y, a.y_dtype, r + 2 * KD + h * kD + d + 3));
       // tree_kernels.py:144-145: x * rsqrt(sum x^2 + 1e-6) (* scale for q)
-      const float rq = 1.f / sqrtf(warp_sum(qv.x * qv.x + qv.y * qv.y + qv.z * qv.z + qv.w * qv.w) + 1e-6f);
-      const float rk = 1.f / sqrtf(warp_sum(kv.x * kv.x + kv.y * kv.y + kv.z * kv.z + kv.w * kv.w) + 1e-6f);
+      const float rq = rsqrtf(warp_sum(qv.x * qv.x + qv.y * qv.y + qv.z * qv.z + qv.w * qv.w) + 1e-6f);
+      const float rk = rsqrtf(warp_sum(kv.x * kv.x + kv.y * kv.y + kv.z * kv.z + kv.w * kv.w) + 1e-6f);
       qv = make_float4(qv.x * rq * scale, qv.y * rq * scale, qv.z * rq * scale, qv.w * rq * scale);
       kv = make_float4(kv.x * rk, kv.y * rk, kv.z * rk, kv.w * rk);
       if (a.aux_k && (a.aux_k_per_v || h % R == 0)) {

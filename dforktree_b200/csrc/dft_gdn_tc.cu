@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int p = 0; p < 2; ++p) {
           float4 y = v[r][p];
           if (n < N) {
-            const float rn = 1.f / sqrtf(ss[r][p] + 1e-6f);   // tree_kernels.py:144-145
+            const float rn = rsqrtf(ss[r][p] + 1e-6f);   // tl.rsqrt, tree_kernels.py:144-145
             y.x *= rn;
             y.y *= rn;
             y.z *= rn;
@@ -600,36 +600,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool zw = warp & 1;
       named_bar(2 + hh, hh ? 128 : 192);   // head hh's C1 is done
       const float* L = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + (zw ? U_AT : U_A));
-      float r[32];
+      // r_i in packed pairs rp[i / 2] = (r_{2k}, r_{2k+1}): each fma.rn.f32x2
+      // performs the two lanes' FMAs of the scalar chains s0 / s1 and s2 / s3
+      // (same operands, same order, same rounding)
+      f32x2 rp[16];
       if (!zw) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = i == lane ? 1.f : 0.f;
+        for (int k = 0; k < 16; ++k) rp[k] = pk2(2 * k == lane ? 1.f : 0.f, 2 * k + 1 == lane ? 1.f : 0.f);
       } else {
         const float* PD = reinterpret_cast<const float*>(smem + OFF_U + hh * kUHead + U_PD);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const float4 q = *reinterpret_cast<const float4*>(PD + sq32(lane, 4 * c));
-          r[31 - 4 * c] = q.x;
-          r[30 - 4 * c] = q.y;
-          r[29 - 4 * c] = q.z;
-          r[28 - 4 * c] = q.w;
+          rp[15 - 2 * c] = pk2(q.y, q.x);   // r[30 - 4c], r[31 - 4c]
+          rp[14 - 2 * c] = pk2(q.w, q.z);   // r[28 - 4c], r[29 - 4c]
         }
       }
       // row i of L in 16-byte chunks: entries at and above the diagonal are
       // zero (L is strictly lower triangular), so whole chunks can be used
 #pragma unroll
       for (int i = 1; i < 32; ++i) {
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        f32x2 s01 = 0ull, s23 = 0ull;
 #pragma unroll
         for (int m = 0; m < i; m += 4) {
           const float4 l4 = *reinterpret_cast<const float4*>(L + sq32(i, m));
-          s0 = fmaf(l4.x, r[m], s0);
-          s1 = fmaf(l4.y, r[m + 1], s1);
-          s2 = fmaf(l4.z, r[m + 2], s2);
-          s3 = fmaf(l4.w, r[m + 3], s3);
+          s01 = fma2(pk2(l4.x, l4.y), rp[m >> 1], s01);
+          s23 = fma2(pk2(l4.z, l4.w), rp[(m >> 1) + 1], s23);
         }
-        r[i] = r[i] - ((s0 + s1) + (s2 + s3));
+        float s0, s1, s2, s3, lo, hi;
+        upk2(s01, s0, s1);
+        upk2(s23, s2, s3);
+        upk2(rp[i >> 1], lo, hi);
+        if (i & 1) hi = hi - ((s0 + s1) + (s2 + s3));
+        else lo = lo - ((s0 + s1) + (s2 + s3));
+        rp[i >> 1] = pk2(lo, hi);
       }
+      float r[32];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) upk2(rp[k], r[2 * k], r[2 * k + 1]);
       if (!mbar_wait(bar_m1[R - 1], ph)) atomicExch(&sm.abort, 1);   // [k; q] is free
       unsigned char* xzh = smem + OFF_KQ + hh * 16384;
       unsigned char* xzl = xzh + 8192;

@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int p = 0; p < 2; ++p) {
           float4 y = v[r][p];
           if (n < N) {
-            const float rn = 1.f / sqrtf(ss[r][p] + 1e-6f);   // tree_kernels.py:144-145
+            const float rn = rsqrtf(ss[r][p] + 1e-6f);   // tl.rsqrt, tree_kernels.py:144-145
             y.x *= rn;
             y.y *= rn;
             y.z *= rn;
