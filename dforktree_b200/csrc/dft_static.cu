@@ -9,6 +9,7 @@
 // dense PMI tensor T) lives here in one file-scope device array of fixed size,
 // held by every GPU that loads the library until the process exits.
 #include "dft_common.cuh"
+#include "dft_ctx.cuh"
 
 #include <cuda.h>
 
@@ -32,21 +33,6 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_score_build_scratch[kStaticScratchBytes];
 
-// cuCtxGetCurrent through the runtime's driver entry point (no -lcuda at link time)
-typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
-
-CtxGetCurrentFn ctx_get_current() {
-  static CtxGetCurrentFn fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      return reinterpret_cast<CtxGetCurrentFn>(p);
-    return static_cast<CtxGetCurrentFn>(nullptr);
-  }();
-  return fn;
-}
-
 std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
 CUcontext g_scratch_ctx[kMaxDevices] = {};
@@ -58,14 +44,9 @@ CUcontext g_scratch_ctx[kMaxDevices] = {};
 // the primary context), it is resolved again in the new one.
 int scratch_for_current_device(void** out) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return DFT_ERR_NO_DEVICE;
-  if (dev >= kMaxDevices) return DFT_ERR_UNSUPPORTED;
-  // make the runtime's context for the device current on this thread before
-  // asking the driver which context that is
-  if (cudaSetDevice(dev) != cudaSuccess) return DFT_ERR_CUDA;
-  CtxGetCurrentFn get_ctx = ctx_get_current();
   CUcontext ctx = nullptr;
-  if (!get_ctx || get_ctx(&ctx) != CUDA_SUCCESS || !ctx) return DFT_ERR_CUDA;
+  if (!dft::current_device_context(&dev, &ctx)) return dev < 0 ? DFT_ERR_NO_DEVICE : DFT_ERR_CUDA;
+  if (dev >= kMaxDevices) return DFT_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_mu);
   if (!g_scratch_ptr[dev] || g_scratch_ctx[dev] != ctx) {
     void* ptr = nullptr;
