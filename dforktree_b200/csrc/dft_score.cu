@@ -6,7 +6,12 @@
 // lane an online (max, sum-exp) pair and per warp a top-16 list distributed
 // over lanes 0..15.  A lane offers a value to the
 // warp list only when it beats the list's current 16th entry, so after the
-// first few hundred elements almost every element costs one compare.
+// first few hundred elements almost every element costs one compare.  The
+// (max, sum-exp) pair is rescaled once per 32-element sweep (its maximum),
+// and the sweep's exponent arguments (x - m) log2 e are formed in packed
+// fp32 pairs (add / mul .f32x2) and summed in pairs: 0.521 -> 0.492 ms for
+// score + build at batch 64 (one vote per sweep instead of one per float4
+// for the top-16 offers measured 0.533, not kept).
 // Order: values descending, equal values by ascending vocabulary index.
 #include "dft_common.cuh"
 
@@ -149,8 +154,36 @@ __global__ void __launch_bounds__(kThreads) score_kernel(const T* __restrict__ l
     float4 vs[8];
 #pragma unroll
     for (int r = 0; r < 8; ++r) vs[r] = load4<T>(x, e + r * stride);
+    // one rescale per sweep (the sweep's maximum), then the 32 exponentials
+    // in packed pairs: exp(x - m) = 2^((x - m) log2 e)
+    float mx4[8];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) online_add4(m, sum, vs[r]);
+    for (int r = 0; r < 8; ++r) mx4[r] = fmaxf(fmaxf(vs[r].x, vs[r].y), fmaxf(vs[r].z, vs[r].w));
+    {
+      const float M = fmaxf(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])),
+                            fmaxf(fmaxf(mx4[4], mx4[5]), fmaxf(mx4[6], mx4[7])));
+      if (M > m) {
+        sum *= __expf(m - M);   // m = -inf initially: exp(-inf) = 0
+        m = M;
+      }
+      if (m != -INFINITY) {
+        const f32x2 nm = pk2(-m, -m), l2e = pk2(-kNegLog2e, -kNegLog2e);
+        f32x2 acc = 0ull;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const f32x2 d01 = mul2(add2(pk2(vs[r].x, vs[r].y), nm), l2e);
+          const f32x2 d23 = mul2(add2(pk2(vs[r].z, vs[r].w), nm), l2e);
+          float a0, a1, a2, a3;
+          upk2(d01, a0, a1);
+          upk2(d23, a2, a3);
+          acc = add2(acc, pk2(ex2_approx(a0), ex2_approx(a1)));
+          acc = add2(acc, pk2(ex2_approx(a2), ex2_approx(a3)));
+        }
+        float lo, hi;
+        upk2(acc, lo, hi);
+        sum += lo + hi;
+      }
+    }
     if (first) {
       // Seed the pruning bound from the first sweep: if at least 16 lanes hold a
       // value >= v, the row's 16th largest is >= v, so smaller values can never
@@ -168,10 +201,7 @@ __global__ void __launch_bounds__(kThreads) score_kernel(const T* __restrict__ l
       bound = fmaxf(bound, seed);
     }
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      float mx = fmaxf(fmaxf(vs[r].x, vs[r].y), fmaxf(vs[r].z, vs[r].w));
-      offer4(L, mx >= L.thr && mx >= bound, vs[r], (int)(e + r * stride), lane);
-    }
+    for (int r = 0; r < 8; ++r) offer4(L, mx4[r] >= L.thr && mx4[r] >= bound, vs[r], (int)(e + r * stride), lane);
     if (lane == 0) reinterpret_cast<volatile float*>(s_thr)[warp] = L.thr;
     float t = reinterpret_cast<volatile float*>(s_thr)[lane & (kWarps - 1)];
 #pragma unroll
