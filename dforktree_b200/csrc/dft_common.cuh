@@ -219,8 +219,11 @@ __device__ __forceinline__ uint32_t fp_byte(uint2 w, int k) { return ((k < 4 ? w
 
 // Probe with fingerprints from bucket `idx` on (fingerprint f of key q):
 // fingerprint bytes decide emptiness and candidates; only a candidate's slot
-// is read.  Returns the matching slot or miss_slot().
-static __device__ __noinline__ uint4 probe_fp_from(const Slot* tab, const uint8_t* fp, unsigned long long mask,
+// is read.  Returns the matching slot or miss_slot().  Inlined: as a call
+// (it is the rare continuation past a bucket group) it made the PMI kernels
+// keep their eight in-flight probes in callee-saved registers (order 3: 72
+// registers and three CTAs per SM; inlined 62 and four): 119 -> ~85 us.
+__device__ __forceinline__ uint4 probe_fp_from(const Slot* tab, const uint8_t* fp, unsigned long long mask,
                                             unsigned long long uq, uint32_t f, unsigned long long idx,
                                             int32_t* status) {
   const uint64_t pol = l2_evict_last_policy();
