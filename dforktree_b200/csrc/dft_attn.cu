@@ -563,26 +563,32 @@ int check_args(const dft_tree_attn_args* a) {
   return DFT_OK;
 }
 
-// Key splits per (request, kv-head): the fewest that fill the SMs' waves to
-// >= 90 % (partials cost 1 KB per row and split, kept in L2 by the merge).
+// Key splits per (request, kv-head).  A unit costs its key tiles plus a fixed
+// part (Q load, first tiles' latency, O readout: about 8 tiles' time), and
+// splits > 1 add the partials' merge (about 12 tiles' time); the persistent
+// CTAs take ceil(units / SMs) units each.  The split count minimising
+//   ceil(pairs * sp / SMs) * (ceil(tiles / sp) + 8) + (sp > 1 ? 12 : 0)
+// is taken (ties: fewer splits).  Measured at batch 64 with 4K prefixes
+// (256 pairs, 65 tiles): 1 split 0.222 ms per layer, 2: 0.276, 3: 0.298,
+// 4: 0.293 (the earlier rule, fill the last wave to >= 90 %, chose 4).  A few
+// requests with long prefixes still split (4 pairs, 65 tiles: 8 splits).
 void plan(const dft_tree_attn_args* a, int* splits, int* tps) {
-  const int tiles = (a->max_kv_len + kKeys - 1) / kKeys;
+  const int64_t tiles = (a->max_kv_len + kKeys - 1) / kKeys;
   const int64_t pairs = (int64_t)a->B * a->Hkv;
-  const int sms = sm_count();
+  const int64_t sms = sm_count();
+  constexpr int64_t kUnitFixed = 8, kMerge = 12;
   int best = 1;
-  double best_eff = 0.0;
+  int64_t best_cost = -1;
   for (int sp = 1; sp <= 8 && sp <= tiles; ++sp) {
-    const int64_t units = pairs * sp;
-    const int64_t waves = (units + sms - 1) / sms;
-    const double eff = (double)units / (double)(waves * sms);
-    if (eff > best_eff + 1e-9) {
-      best_eff = eff;
+    const int64_t per = (pairs * sp + sms - 1) / sms;
+    const int64_t cost = per * ((tiles + sp - 1) / sp + kUnitFixed) + (sp > 1 ? kMerge : 0);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
       best = sp;
     }
-    if (eff >= 0.9) break;
   }
   *splits = best;
-  *tps = (tiles + best - 1) / best;
+  *tps = (int)((tiles + best - 1) / best);
 }
 
 }  // namespace

@@ -70,7 +70,7 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("B,N,Hq,Hkv,plens", [
-    (3, 32, 16, 4, [100, 1000, 37]),      # Qwen3.5 attention heads, splits > 1
+    (3, 32, 16, 4, [100, 3000, 37]),      # Qwen3.5 attention heads, splits > 1 (8: 12 pairs, 48 tiles)
     (2, 32, 16, 4, [5, 20]),              # <= 64 keys: one split, direct output
     (2, 16, 16, 4, [300, 64]),            # N = 16: query rows 64..127 padded
     (2, 32, 8, 4, [200, 129]),            # G = 2
