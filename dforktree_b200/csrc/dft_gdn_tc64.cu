@@ -737,8 +737,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     }
-    // ------------------------------------------------ E2: vn and o = e^G (q S0) + Z R (warps 8-15)
-    if (warp >= 8) {
+    // ------------------------------------------------ E2: vn and o = e^G (q S0) + Z R (warps 0-7,
+    // after their C2; warps 8-13 are converting the next unit's tile meanwhile)
+    if (warp < 8) {
       if (!mbar_wait(bar_m2, ph)) atomicExch(&sm.abort, 1);
       tc_fence_after();
       const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
