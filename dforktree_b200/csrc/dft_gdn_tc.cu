@@ -81,7 +81,9 @@ struct Small {
   // per-unit inputs, double-buffered: unit u uses buffer (its ordinal) % 2
   // while the next unit's are prepared in the other
   uint32_t anc[2][kNP];            // bit j: j is i or an ancestor of i
-  uint32_t taps[2][kNP];           // tile rows of conv taps 0..2 (one byte each; tap 3 is the node)
+  // byte offsets, within one activation part, of the rows that conv taps
+  // 0..2 and 3 (the node itself) read: conv-state rows 0..2, node rows 3..
+  __align__(16) uint4 taps[2][kNP];
   __align__(16) float G[2][2][kNP];   // [buffer][v-head][node]
   __align__(16) float beta[2][2][kNP];
   __align__(16) float eG[2][2][kNP];
@@ -163,7 +165,7 @@ __device__ __forceinline__ void prep_unit(const dft_gdn_args& a, const dft_gdn_c
   if (role == 2) {
     sm.anc[buf][n] = m;
     if (CONV) {
-      uint32_t packed = 0;
+      uint32_t row[3] = {0u, 0u, 0u};
       if (n < N) {
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
@@ -172,11 +174,12 @@ __device__ __forceinline__ void prep_unit(const dft_gdn_args& a, const dft_gdn_c
             raise_status(status, DFT_DEV_BAD_INDEX);
             c = 3 + n;
           }
-          packed |= (uint32_t)c << (8 * j);
+          row[j] = (uint32_t)c;
         }
         if (c4[3] != 3 + n) raise_status(status, DFT_DEV_BAD_INDEX);   // tap 3 is the node itself
       }
-      sm.taps[buf][n] = packed;
+      constexpr uint32_t kRowBytes = kD * 2;
+      sm.taps[buf][n] = make_uint4(row[0] * kRowBytes, row[1] * kRowBytes, row[2] * kRowBytes, (3u + n) * kRowBytes);
     }
   } else if (hl < R) {
     // g, beta, G = sum of g over the ancestors in ascending order (tree_kernels.py:146-153)
@@ -363,9 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // one node: its three taps and itself (raw bf16 pairs), then products and
       // sums rounded in order j = 0..3 (fc1_conv.py:20), bias, SiLU, bf16
       auto load = [&](int n) -> uint4 {
-        const uint32_t tp = sm.taps[cbuf][n];
-        return make_uint4(ld_s32(colp + (int)(tp & 0xFFu) * kRowB), ld_s32(colp + (int)((tp >> 8) & 0xFFu) * kRowB),
-                          ld_s32(colp + (int)((tp >> 16) & 0xFFu) * kRowB), ld_s32(colp + (3 + n) * kRowB));
+        const uint4 tp = sm.taps[cbuf][n];   // one 16-byte broadcast load: the four row offsets
+        return make_uint4(ld_s32(colp + tp.x), ld_s32(colp + tp.y), ld_s32(colp + tp.z), ld_s32(colp + tp.w));
       };
       auto node = [&](uint4 in) -> uint32_t {
         f32x2 acc = mul2(bf16x2_to_f32x2(in.x), w0);
@@ -767,24 +769,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
       const int h = hk * R + hh, v = tid & 127;
-      float* gv = a.aux_vn ? a.aux_vn + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh + v : nullptr;
-      T* go = reinterpret_cast<T*>(a.o) + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + v;
+      // per-node output pointers advance by the node strides (one 64-bit add
+      // per store rather than an index multiply); vn and o rows of nodes >= N
+      // are not written
+      char* gvp = a.aux_vn ? reinterpret_cast<char*>(a.aux_vn + (int64_t)b * a.av_sb + (int64_t)h * a.av_sh + v) : nullptr;
+      char* gop = reinterpret_cast<char*>(reinterpret_cast<T*>(a.o) + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + v);
+      const int64_t vstep = a.av_sn * (int64_t)sizeof(float), ostep = a.o_sn * (int64_t)sizeof(T);
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
         float vn[16], zr[16], qs[16];
         tmem_ld16(tmem + lanes + COL_M2 + 64 * hh + 16 * half, vn);
         tmem_ld16(tmem + lanes + COL_M2 + 64 * hh + 32 + 16 * half, zr);
         tmem_ld16(tmem + lanes + COL_M1 + 64 * hh + 32 + 16 * half, qs);
+        const int nv = N - 16 * half;   // nodes of this half that exist (uniform)
+        float ov[16];
 #pragma unroll
         for (int e4 = 0; e4 < 16; e4 += 4) {
           const float4 eg4 = *reinterpret_cast<const float4*>(&sm.eG[cb][hh][16 * half + e4]);
-          const float* eg = &eg4.x;
+          ov[e4] = eg4.x * qs[e4] + zr[e4];
+          ov[e4 + 1] = eg4.y * qs[e4 + 1] + zr[e4 + 1];
+          ov[e4 + 2] = eg4.z * qs[e4 + 2] + zr[e4 + 2];
+          ov[e4 + 3] = eg4.w * qs[e4 + 3] + zr[e4 + 3];
+        }
+        if (nv >= 16) {
+          if (gvp) {
 #pragma unroll
-          for (int e = e4; e < e4 + 4; ++e) {
-            const int n = 16 * half + e;
-            if (n < N) {
-              if (gv) gv[(int64_t)n * a.av_sn] = vn[e];
-              go[(int64_t)n * a.o_sn] = __float2bfloat16_rn(eg[e - e4] * qs[e] + zr[e]);
+            for (int e = 0; e < 16; ++e, gvp += vstep) *reinterpret_cast<float*>(gvp) = vn[e];
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e, gop += ostep) *reinterpret_cast<T*>(gop) = __float2bfloat16_rn(ov[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if (e < nv) {
+              if (gvp) *reinterpret_cast<float*>(gvp + e * vstep) = vn[e];
+              *reinterpret_cast<T*>(gop + e * ostep) = __float2bfloat16_rn(ov[e]);
             }
           }
         }
