@@ -648,6 +648,59 @@ __global__ void accept_greedy_kernel(int B, int N, int P, const int64_t* __restr
   if (bonus) bonus[b] = target[bN + cur];
 }
 
+// The same walk for trees of at most kMaxNodes nodes, one warp per request:
+// the warp first stages the request's tokens / first children / siblings /
+// targets in shared memory with coalesced loads (all in flight at once), so
+// the dependent steps of the walk read shared memory instead of making one
+// global round trip each.
+__global__ void __launch_bounds__(128) accept_greedy_staged(int B, int N, int P, const int64_t* __restrict__ tokens,
+                                                            const int64_t* __restrict__ nxt,
+                                                            const int64_t* __restrict__ sib,
+                                                            const int64_t* __restrict__ target, int64_t* path,
+                                                            int64_t* accept_len, int64_t* last, int64_t* bonus,
+                                                            int32_t* st) {
+  __shared__ long long s_tok[4][kMaxNodes], s_nxt[4][kMaxNodes], s_sib[4][kMaxNodes], s_tgt[4][kMaxNodes];
+  const int wl = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * 4 + wl;
+  if (b >= B) return;   // the whole warp
+  const int64_t bN = (int64_t)b * N;
+  for (int i = lane; i < N; i += 32) {
+    s_tok[wl][i] = tokens[bN + i];
+    s_nxt[wl][i] = nxt[bN + i];
+    s_sib[wl][i] = sib[bN + i];
+    s_tgt[wl][i] = target[bN + i];
+  }
+  __syncwarp();
+  if (lane != 0) return;
+  int cur = 0, n = 0;
+  if (P > 0) path[(int64_t)b * P + n] = 0;
+  ++n;
+  for (int guard = 0; guard < N; ++guard) {
+    const long long want = s_tgt[wl][cur];
+    long long c = s_nxt[wl][cur];
+    int found = -1;
+    for (int g2 = 0; c >= 0 && g2 < N; ++g2) {
+      if (c >= N) {
+        raise_status(st, DFT_DEV_BAD_INDEX);
+        break;
+      }
+      if (s_tok[wl][c] == want) {
+        found = (int)c;
+        break;
+      }
+      c = s_sib[wl][c];
+    }
+    if (found < 0) break;
+    cur = found;
+    if (n < P) path[(int64_t)b * P + n] = cur;
+    ++n;
+  }
+  for (int i = n; i < P; ++i) path[(int64_t)b * P + i] = -1;
+  if (accept_len) accept_len[b] = n;
+  if (last) last[b] = cur;
+  if (bonus) bonus[b] = s_tgt[wl][cur];
+}
+
 }  // namespace
 
 extern "C" int dft_tree_struct(int32_t B, int32_t N, const int64_t* parent, float* anc, int64_t* depth, int64_t* cidx,
@@ -664,8 +717,12 @@ extern "C" int dft_accept_greedy(int32_t B, int32_t N, int32_t P, const int64_t*
                                  const int64_t* sib, const int64_t* target, int64_t* path, int64_t* accept_len,
                                  int64_t* last, int64_t* bonus, int32_t* dev_status, void* stream) {
   if (B <= 0 || N < 1 || P < 1 || !tokens || !nxt || !sib || !target || !path) return DFT_ERR_INVALID;
-  accept_greedy_kernel<<<(B + 127) / 128, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      B, N, P, tokens, nxt, sib, target, path, accept_len, last, bonus, dev_status);
+  if (N <= kMaxNodes)
+    accept_greedy_staged<<<(B + 3) / 4, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        B, N, P, tokens, nxt, sib, target, path, accept_len, last, bonus, dev_status);
+  else
+    accept_greedy_kernel<<<(B + 127) / 128, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        B, N, P, tokens, nxt, sib, target, path, accept_len, last, bonus, dev_status);
   DFT_LAUNCH_CHECK();
   return DFT_OK;
 }
