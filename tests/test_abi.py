@@ -147,3 +147,27 @@ def test_table_file_header_is_checked_before_any_device_work(lib, tmp_path):
         p.write_bytes(blob)
         assert lib.dft_table_load(str(p).encode(), ctypes.byref(h), None) == 7, i
         assert not h.value
+
+
+def test_tree_attention_split_plan():
+    """Key splits of dft_tree_attn (host logic, no device): one split -- no
+    partials workspace -- when the (request, kv-head) pairs already fill the
+    SMs (batch 64 x 4 kv-heads with 4K prefixes), several for a few requests
+    with long prefixes (their partials need a workspace), and none for short
+    prefixes, where a unit's fixed cost outweighs the parallelism.  The
+    pointers are placeholders: the plan reads only the shapes and strides."""
+    from dforktree_b200 import _lib as L
+    lib = L.load()
+    fake = 0x10000
+    D, Hq, Hkv, N = 256, 16, 4, 32
+
+    def ws(B, max_len):
+        a = L.TreeAttnArgs(B=B, N=N, Hq=Hq, Hkv=Hkv, D=D, q=fake, q_sb=N * Hq * D, q_sn=Hq * D, q_sh=D,
+                           k_cache=fake, v_cache=fake, kv_st=Hkv * D, kv_sh=D, n_slots=1 << 20,
+                           kv_indptr=fake, kv_indices=fake, anc=fake, anc_sb=N * N, sm_scale=0.0625,
+                           max_kv_len=max_len, o=fake, o_sb=N * Hq * D, o_sn=Hq * D, o_sh=D)
+        return lib.dft_tree_attn_workspace_bytes(ctypes.byref(a))
+
+    assert ws(64, 4096 + N) == 0            # 256 pairs: one split
+    assert ws(1, 4096 + N) > 0              # 4 pairs, 65 key tiles: split
+    assert ws(2, 100 + N) == 0              # 3 key tiles: one split
