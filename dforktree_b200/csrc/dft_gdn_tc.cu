@@ -567,15 +567,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t keep = pd ? sm.anc[cb][i] : sm.anc[cb][i] & ~(1u << i);
       const float Gi = sm.G[cb][hh][i], ci = pd ? 1.f : sm.beta[cb][hh][i];
       float* dst = reinterpret_cast<float*>(smem + OFF_U + hh * kUHead + (pd ? U_PD : U_A));
+      // e^{G_i - G_j} = 2^((G_i - G_j) log2 e), the differences and products in packed pairs
+      const f32x2 gi2 = pk2(Gi, Gi), l2e = pk2(-kNegLog2e, -kNegLog2e), ci2 = pk2(ci, ci);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int j0 = 16 * half + 4 * c;
         const float4 gj = *reinterpret_cast<const float4*>(&sm.G[cb][hh][j0]);
+        float a0, a1, a2, a3, p0, p1, p2, p3;
+        upk2(mul2(sub2(gi2, pk2(gj.x, gj.y)), l2e), a0, a1);
+        upk2(mul2(sub2(gi2, pk2(gj.z, gj.w)), l2e), a2, a3);
+        upk2(mul2(mul2(ci2, pk2(kk[4 * c], kk[4 * c + 1])), pk2(ex2_approx(a0), ex2_approx(a1))), p0, p1);
+        upk2(mul2(mul2(ci2, pk2(kk[4 * c + 2], kk[4 * c + 3])), pk2(ex2_approx(a2), ex2_approx(a3))), p2, p3);
         float4 o;
-        o.x = ((keep >> j0) & 1u) ? ci * kk[4 * c] * __expf(Gi - gj.x) : 0.f;
-        o.y = ((keep >> (j0 + 1)) & 1u) ? ci * kk[4 * c + 1] * __expf(Gi - gj.y) : 0.f;
-        o.z = ((keep >> (j0 + 2)) & 1u) ? ci * kk[4 * c + 2] * __expf(Gi - gj.z) : 0.f;
-        o.w = ((keep >> (j0 + 3)) & 1u) ? ci * kk[4 * c + 3] * __expf(Gi - gj.w) : 0.f;
+        o.x = ((keep >> j0) & 1u) ? p0 : 0.f;
+        o.y = ((keep >> (j0 + 1)) & 1u) ? p1 : 0.f;
+        o.z = ((keep >> (j0 + 2)) & 1u) ? p2 : 0.f;
+        o.w = ((keep >> (j0 + 3)) & 1u) ? p3 : 0.f;
         *reinterpret_cast<float4*>(dst + sq32(i, j0)) = o;
         if (!pd) {
           // A'[31 - j][31 - i] = A[i][j]: lane i writes column 31 - i of four rows
@@ -700,15 +707,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 4; ++c) {
           const float4 be4 = *reinterpret_cast<const float4*>(&sm.beta[cb][hh][16 * half + 4 * c]);
           const float4 eg4 = *reinterpret_cast<const float4*>(&sm.eG[cb][hh][16 * half + 4 * c]);
-          const float* be = &be4.x;
-          const float* eg = &eg4.x;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
+          for (int e = 0; e < 4; e += 2) {
             const int n = 16 * half + 4 * c + e;
-            const float rr = be[e] * (to_f32(yv[n * kD]) - eg[e] * ks_[n]);
-            const float h = tf32_rna(rr);
-            hi[4 * c + e] = __float_as_uint(h);
-            lo[4 * c + e] = __float_as_uint(tf32_rna(rr - h));
+            const float be0 = e ? be4.z : be4.x, be1 = e ? be4.w : be4.y;
+            const float eg0 = e ? eg4.z : eg4.x, eg1 = e ? eg4.w : eg4.y;
+            // rr = beta (v - e^G (k S0)) for nodes n, n + 1 in packed pairs
+            const f32x2 d = fma2(pk2(-eg0, -eg1), pk2(ks_[n], ks_[n + 1]), pk2(to_f32(yv[n * kD]), to_f32(yv[(n + 1) * kD])));
+            float r0, r1;
+            upk2(mul2(pk2(be0, be1), d), r0, r1);
+            const float h0 = tf32_rna(r0), h1 = tf32_rna(r1);
+            float l0, l1;
+            upk2(sub2(pk2(r0, r1), pk2(h0, h1)), l0, l1);
+            hi[4 * c + e] = __float_as_uint(h0);
+            hi[4 * c + e + 1] = __float_as_uint(h1);
+            lo[4 * c + e] = __float_as_uint(tf32_rna(l0));
+            lo[4 * c + e + 1] = __float_as_uint(tf32_rna(l1));
           }
         }
         tmem_st16(tmem + lanes + COL_RT + 64 * hh + 16 * half, hi);
