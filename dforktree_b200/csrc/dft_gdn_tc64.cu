@@ -568,15 +568,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const unsigned long long keep = pd ? sm.anc[cb][i] : sm.anc[cb][i] & ~(1ull << i);
         const float Gi = sm.G[cb][i], ci = pd ? 1.f : sm.beta[cb][i];
         float* dst = reinterpret_cast<float*>(smem + OFF_U + (pd ? U_PD : U_A));
+        // e^{G_i - G_j} = 2^((G_i - G_j) log2 e), the differences and products in packed pairs
+        const f32x2 gi2 = pk2(Gi, Gi), l2e = pk2(-kNegLog2e, -kNegLog2e), ci2 = pk2(ci, ci);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const int j0 = 32 * half + 4 * c;
           const float4 gj = *reinterpret_cast<const float4*>(&sm.G[cb][j0]);
+          float a0, a1, a2, a3, p0, p1, p2, p3;
+          upk2(mul2(sub2(gi2, pk2(gj.x, gj.y)), l2e), a0, a1);
+          upk2(mul2(sub2(gi2, pk2(gj.z, gj.w)), l2e), a2, a3);
+          upk2(mul2(mul2(ci2, pk2(kk[4 * c], kk[4 * c + 1])), pk2(ex2_approx(a0), ex2_approx(a1))), p0, p1);
+          upk2(mul2(mul2(ci2, pk2(kk[4 * c + 2], kk[4 * c + 3])), pk2(ex2_approx(a2), ex2_approx(a3))), p2, p3);
           float4 o;
-          o.x = ((keep >> j0) & 1ull) ? ci * kk[4 * c] * __expf(Gi - gj.x) : 0.f;
-          o.y = ((keep >> (j0 + 1)) & 1ull) ? ci * kk[4 * c + 1] * __expf(Gi - gj.y) : 0.f;
-          o.z = ((keep >> (j0 + 2)) & 1ull) ? ci * kk[4 * c + 2] * __expf(Gi - gj.z) : 0.f;
-          o.w = ((keep >> (j0 + 3)) & 1ull) ? ci * kk[4 * c + 3] * __expf(Gi - gj.w) : 0.f;
+          o.x = ((keep >> j0) & 1ull) ? p0 : 0.f;
+          o.y = ((keep >> (j0 + 1)) & 1ull) ? p1 : 0.f;
+          o.z = ((keep >> (j0 + 2)) & 1ull) ? p2 : 0.f;
+          o.w = ((keep >> (j0 + 3)) & 1ull) ? p3 : 0.f;
           *reinterpret_cast<float4*>(dst + sq64(i, j0)) = o;
         }
       }
@@ -677,12 +684,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float* be = &be4.x;
           const float* eg = &eg4.x;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int n = n0 + e;
-            const float rr = be[e] * (to_f32(yv[n * kD]) - eg[e] * ks_[16 * c16 + 4 * c + e]);
-            const float hh = tf32_rna(rr);
-            hi[4 * c + e] = __float_as_uint(hh);
-            lo[4 * c + e] = __float_as_uint(tf32_rna(rr - hh));
+          for (int e = 0; e < 4; e += 2) {
+            const int n = n0 + e, kx = 16 * c16 + 4 * c + e;
+            // rr = beta (v - e^G (k S0)) for nodes n, n + 1 in packed pairs
+            const f32x2 d = fma2(pk2(-eg[e], -eg[e + 1]), pk2(ks_[kx], ks_[kx + 1]),
+                                 pk2(to_f32(yv[n * kD]), to_f32(yv[(n + 1) * kD])));
+            float r0, r1;
+            upk2(mul2(pk2(be[e], be[e + 1]), d), r0, r1);
+            const float h0 = tf32_rna(r0), h1 = tf32_rna(r1);
+            float l0, l1;
+            upk2(sub2(pk2(r0, r1), pk2(h0, h1)), l0, l1);
+            hi[4 * c + e] = __float_as_uint(h0);
+            hi[4 * c + e + 1] = __float_as_uint(h1);
+            lo[4 * c + e] = __float_as_uint(tf32_rna(l0));
+            lo[4 * c + e + 1] = __float_as_uint(tf32_rna(l1));
           }
         }
         tmem_st16(tmem + lanes + COL_RT + 32 * nh + 16 * c16, hi);
