@@ -32,7 +32,8 @@
 //   E1 R = beta (v - e^G (k S0)) -> R^T hi / lo in TMEM (alongside C1 / C2)
 //   M2 D2 = R^T [X; Z]^T   -> vn^T, (Z R)^T, issued once every warp has
 //      arrived on an mbarrier (operands ready) rather than at a CTA barrier
-//   E2 o = e^G (q S0) + Z R, vn -> global memory
+//   E2 o = e^G (q S0) + Z R, vn -> global memory, by warps 0-7 after their C2
+//      (warps 8-13 are converting the next unit's tile meanwhile)
 // Every wait is bounded (~1 s); on timeout the CTA raises DFT_DEV_TIMEOUT,
 // drains what it issued (bounded), frees TMEM and exits.
 #include "dft_common.cuh"
