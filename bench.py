@@ -682,8 +682,8 @@ def _bench_attention(args, dev, cyc, g, stream):
 def _bench_verify_n64(args, dev, table, stream):
     """Tree conv + GDN verify of one layer at the plugin's default tree size,
     64 nodes (fc1_fused.py:4, FC1_TREE_N), on the bench's batch and layer
-    shape: the CUDA-core verifier (the tensor-core one takes up to 32 nodes)
-    behind a separate tree-conv launch.  Mean CUDA-event time per layer over
+    shape: the 33-64-node tensor-core verifier with its tree conv fused in
+    (one launch per layer).  Mean CUDA-event time per layer over
     two alternating layers (states 128 MiB per layer: no L2 reuse)."""
     import torch
     from dforktree_b200 import workload as WL

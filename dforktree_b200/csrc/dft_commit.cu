@@ -18,10 +18,6 @@ constexpr int kD = 128;
 constexpr int kThreads = 256;
 constexpr int kMaxPath = 64;
 
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 // ahead: the block `ahead` launches later (about two waves) has its path rows
 // of k and vn prefetched into L2 by this block's warp 0, so that its own
 // dependent row loads (after the path set-up) hit L2 instead of DRAM.

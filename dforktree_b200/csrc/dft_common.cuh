@@ -152,6 +152,11 @@ __device__ __forceinline__ f32x2 silu_hw2(f32x2 x) {
   return mul2(x, pk2(rcp_approx(d0), rcp_approx(d1)));
 }
 
+// bytes at p (16-byte aligned, a multiple of 16) into L2; nothing waits for it
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // ------------------------------------------------------------ status word --
 __device__ __forceinline__ void raise_status(int32_t* st, int bits) {
   if (st) atomicOr(st, bits);

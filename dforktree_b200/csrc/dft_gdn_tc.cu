@@ -9,7 +9,8 @@
 // side by side on disjoint warps and buffers.  Per unit:
 //   F  the unit's bf16 activation tile (pre-conv x, or y) is in shared memory
 //      and already converted: the first unit's arrives by TMA and is
-//      converted at the top of the loop; every later unit's is gathered by
+//      converted at the top of the loop; every later unit's is prefetched
+//      into L2 by warp 7 during the previous unit's C1, gathered from there by
 //      the conv threads (16-byte cp.async) and converted at the end of the
 //      previous unit, while warps 8+ run that unit's M2 and E2.  Tree conv in
 //      place, one thread per channel pair in packed fp32x2 arithmetic, nodes
@@ -551,6 +552,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 10 || warp == 11 || warp == 14) {
       const int nu = u + gridDim.x;
       if (nu < units) prep_unit<R, CONV>(a, ta.cv, sm, status, nu, cb ^ 1, warp == 14 ? 2 : warp - 10, lane);
+    }
+    // ------------------------------------------------ the next unit's pre-conv rows into L2 (warp 7, idle until E1)
+    // so that the conv threads' gather at the end of this unit reads L2, not DRAM
+    if (CONV && warp == 7) {
+      const int nu = u + gridDim.x;
+      if (nu < units && lane < N) {
+        const int nb = nu / Hk, nhk = nu % Hk;
+        const unsigned char* xr =
+            static_cast<const unsigned char*>(ta.cv.x) + ((int64_t)nb * ta.cv.x_sb + (int64_t)lane * ta.cv.x_sn) * 2;
+#pragma unroll
+        for (int p = 0; p < 2 + R; ++p) prefetch_l2(xr + part_channel(p, nhk, Hk, R) * 2, 256u);
+      }
     }
     // ------------------------------------------------ C1: A and PD of every head (8 warps)
     // warp w: rows from TMEM lanes 32 (w % 4) (k.k^T for w % 4 == 0, q.k^T for 1),
