@@ -101,6 +101,7 @@ struct BeamArgs {
 template <int P>
 __global__ void __launch_bounds__(P) beam_kernel(BeamArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
+  pdl_wait();   // lp / ids / rest / T come from the preceding kernels
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
   const int S = a.S, N = a.N, W = a.W;
@@ -490,9 +491,8 @@ int launch_beam(const BeamArgs& a, cudaStream_t st) {
     if (cudaFuncSetAttribute(beam_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
       return DFT_ERR_CUDA;
   }
-  beam_kernel<P><<<a.B, P, sm, st>>>(a);
-  DFT_LAUNCH_CHECK();
-  return DFT_OK;
+  // programmatic launch: set up while the PMI (or score) kernel drains
+  return launch_pdl(beam_kernel<P>, dim3(a.B), dim3(P), sm, st, a);
 }
 
 }  // namespace

@@ -626,6 +626,7 @@ __global__ void __launch_bounds__(256, 3) pmi_dense_kernel(TableView t, int S, c
                                                         const int64_t* __restrict__ root,
                                                         const int64_t* __restrict__ pre1, float* __restrict__ T,
                                                         int32_t* st) {
+  pdl_wait();   // ids (and root / pre1) may come from the preceding kernel
   const int tstep = blockIdx.x;  // 0 .. S-2
   const int req = blockIdx.y;
   const int tid = threadIdx.x;
@@ -700,6 +701,7 @@ __global__ void __launch_bounds__(256, 3) pmi_dense_kernel(TableView t, int S, c
 // (tree_ops.py:59-60); one thread per entry.
 __global__ void __launch_bounds__(256) pmi_dense2_kernel(TableView t, int S, const int32_t* __restrict__ ids,
                                                          float* __restrict__ T, int32_t* st) {
+  pdl_wait();   // ids may come from the preceding kernel
   const int tstep = blockIdx.x, req = blockIdx.y, tid = threadIdx.x;
   const int32_t* idr = ids + (int64_t)req * S * kM;
   const long long b = idr[tstep * kM + (tid >> 4)], c = idr[(tstep + 1) * kM + (tid & 15)];
@@ -739,6 +741,7 @@ __global__ void __launch_bounds__(kP4Threads, 2) pmi_dense4_kernel(TableView t, 
                                                                 float* __restrict__ T, int32_t* st) {
   extern __shared__ __align__(16) unsigned char p4_raw[];
   P4Smem& sm = *reinterpret_cast<P4Smem*>(p4_raw);
+  pdl_wait();   // ids (and root / pre1) may come from the preceding kernel
   const int tstep = blockIdx.x, req = blockIdx.y, tid = threadIdx.x;
   const int32_t* idr = ids + (int64_t)req * S * kM;
   if (tid < kM) {
@@ -858,16 +861,22 @@ int dft_pmi_dense_launch(const dft_table* table, const dft_build_params* p, cons
   dim3 grid(p->S - 1, p->B);
   const int order = dft::pmi_order_of(p);
   if (order == 2) {
-    pmi_dense2_kernel<<<grid, 256, 0, st>>>(table->view, p->S, ids, T, dev_status);
+    // programmatic launches: set up while the score kernel drains
+    if (launch_pdl(pmi_dense2_kernel, grid, dim3(256), 0, st, table->view, p->S, ids, T, dev_status) != DFT_OK)
+      return DFT_ERR_CUDA;
   } else if (order == 3) {
-    pmi_dense_kernel<<<grid, 256, 0, st>>>(table->view, p->S, ids, root, pre1, T, dev_status);
+    if (launch_pdl(pmi_dense_kernel, grid, dim3(256), 0, st, table->view, p->S, ids, root, pre1, T, dev_status) !=
+        DFT_OK)
+      return DFT_ERR_CUDA;
   } else {
     if (!pre1) return DFT_ERR_INVALID;   // E[0] = pre1 is order 4's first context token
     static_assert(sizeof(P4Smem) <= 227 * 1024, "order-4 PMI shared memory");
     if (cudaFuncSetAttribute(pmi_dense4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(P4Smem)) !=
         cudaSuccess)
       return DFT_ERR_CUDA;
-    pmi_dense4_kernel<<<grid, kP4Threads, sizeof(P4Smem), st>>>(table->view, p->S, ids, root, pre1, T, dev_status);
+    if (launch_pdl(pmi_dense4_kernel, grid, dim3(kP4Threads), sizeof(P4Smem), st, table->view, p->S, ids, root, pre1,
+                   T, dev_status) != DFT_OK)
+      return DFT_ERR_CUDA;
   }
   DFT_LAUNCH_CHECK();
   return DFT_OK;
