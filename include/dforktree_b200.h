@@ -158,7 +158,9 @@ DFT_API int dft_beam_build(const dft_build_params* p, const float* lp, const int
                    const float* T, const float* logc, const float* c0, const int64_t* root,
                    dft_tree_out* out, int32_t* dev_status, void* stream);
 
-/* Whole score+build (Builder.run, fc1_builder.py:26-47) in three launches.
+/* Whole score+build (Builder.run, fc1_builder.py:26-47) in three launches;
+ * the PMI and beam launches use programmatic stream serialisation and wait
+ * for the preceding kernel before their first read (stream order unchanged).
  * workspace: dft_score_build_workspace_bytes(p) bytes of device memory.    */
 DFT_API int64_t dft_score_build_workspace_bytes(const dft_build_params* p);
 DFT_API int dft_score_build(const dft_table* table, const dft_build_params* p, const void* logits, int32_t logits_dtype,
